@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""Benchmark of the fused softmax-weighted embedding readout, forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
+
+Workload (the headline): bf16, N=16384 tokens, K=2560, V=152064, D=64,
+bias ~ N(0, 0.02), Bernoulli(0.9) 0/1 per-token weight, z_loss_weight=1e-4, MSE loss,
+fwd+bwd through the public API (``swvr_b200.softmax_readout_mse``).  Inputs are seeded
+synthetic tensors with the config's distributions (no dataset is involved); W ~ N(0, 1/K)
+is read as variance 1/K (std K^-1/2).  At N GPUs the vocabulary is sharded (V/N rows of
+W, E and b per rank, ``swvr_b200.vocab_parallel``): strong scaling of a fixed problem.
+W alone (778 MB bf16) is larger than the 126 MB L2, so every step streams from HBM; no
+extra L2 flush is needed.
+
+One JSON line on rank 0.  ``value`` is the whole job's algorithmic TFLOP/s,
+F_algo = 6 N V (K + D) per step (the backward score recompute is not counted).
+``--impl reference`` times the reference algorithm on the host CPU instead (the numpy port
+of swvr's chunked path, oracle/swvr_oracle.py) on a bounded vocabulary slice.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: N, K, V, D, bias, weight (Bernoulli p), z_loss_weight, logit_scale
+    "c1": dict(N=16384, K=1024, V=152064, D=16, bias=False, weight=None, z=0.0),
+    "c2": dict(N=16384, K=2560, V=152064, D=64, bias=True, weight=0.9, z=1e-4),
+    "c3": dict(N=8192, K=4096, V=128256, D=128, bias=False, weight=None, z=0.0),
+}
+
+
+def f_algo(c, V=None):
+    V = c["V"] if V is None else V
+    return 6.0 * c["N"] * V * (c["K"] + c["D"])
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.proc = None
+        self.out = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.out), exist_ok=True)
+            self.f = open(self.out, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", self.gpu, "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+        return False
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.out) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+                "reasons": reasons}
+
+
+def make_inputs(c, device, rank, world):
+    """Seeded synthetic inputs; at world > 1 this rank's vocabulary shard of W, E, b."""
+    from swvr_b200.vocab_parallel import shard_range
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    N, K, V, D = c["N"], c["K"], c["V"], c["D"]
+    v0, v1 = shard_range(V, world, rank)
+    Vr = v1 - v0
+    gshared = torch.Generator(device=device).manual_seed(99)  # h, target and weight are replicated
+    h = torch.randn(N, K, generator=gshared, device=device).to(torch.bfloat16)
+    t = 0.02 * torch.randn(N, D, generator=gshared, device=device)
+    w = (torch.rand(N, generator=gshared, device=device) < c["weight"]).float() if c["weight"] else None
+    W = (K ** -0.5 * torch.randn(Vr, K, generator=g, device=device)).to(torch.bfloat16).requires_grad_(True)
+    E = (0.02 * torch.randn(Vr, D, generator=g, device=device)).to(torch.bfloat16).requires_grad_(True)
+    b = (0.02 * torch.randn(Vr, generator=g, device=device)).to(torch.bfloat16).requires_grad_(True) \
+        if c["bias"] else None
+    return h.requires_grad_(True), W, E, b, t, w, Vr
+
+
+def run_ours(args, c, rank, world, device):
+    import swvr_b200 as swvr
+    from swvr_b200 import _native
+    from swvr_b200 import vocab_parallel as vp
+
+    h, W, E, b, t, w, Vr = make_inputs(c, device, rank, world)
+    params = [x for x in (h, W, E, b) if x is not None]
+    kw = dict(weight=w, z_loss_weight=c["z"], chunk_size=args.chunk)
+
+    def step(hh, tt, ww):
+        for p in params:
+            p.grad = None
+        hh.grad = None
+        if world == 1:
+            loss = swvr.softmax_readout_mse(hh, W, E, tt, b, weight=ww, z_loss_weight=c["z"], chunk_size=args.chunk)
+        else:
+            loss = vp.softmax_readout_mse_vocab_parallel(hh, W, E, tt, b, weight=ww, z_loss_weight=c["z"],
+                                                         chunk_size=args.chunk)
+        loss.backward()
+        return loss
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        step(h, t, w)
+    torch.cuda.synchronize(device)
+    _native.check_device_error()
+    torch.cuda.reset_peak_memory_stats(device)
+    base = torch.cuda.memory_allocated(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---------------------------------------------------------------- device-resident timing
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks, _native.profile() as prof:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step(h, t, w)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    peak_gib = (torch.cuda.max_memory_allocated(device) - base) / 2 ** 30
+    _native.check_device_error()
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    h_host = h.detach().cpu().pin_memory()
+    t_host = t.cpu().pin_memory()
+    w_host = w.cpu().pin_memory() if w is not None else None
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    h_dev = torch.empty_like(h).requires_grad_(False)
+    t_dev = torch.empty_like(t)
+    w_dev = torch.empty_like(w) if w is not None else None
+    h2d = h_host.numel() * h_host.element_size() + t_host.numel() * 4 + (w_host.numel() * 4 if w is not None else 0)
+
+    def e2e_step():
+        h_dev.copy_(h_host, non_blocking=True)
+        t_dev.copy_(t_host, non_blocking=True)
+        if w_dev is not None:
+            w_dev.copy_(w_host, non_blocking=True)
+        hh = h_dev.detach().requires_grad_(True)
+        loss = step(hh, t_dev, w_dev)
+        loss_host.copy_(loss.detach(), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+
+    # max over ranks
+    t_local = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = t_local.tolist()
+    return dict(ms=ms, ms_e2e=ms_e2e, prof=prof.result, clocks=clocks.summary(), peak_gib=peak_gib, h2d=h2d,
+                loss=float(loss_host), Vr=Vr)
+
+
+def kernel_flops(name, c, Vr, launches_per_step, chunk):
+    """Algorithmic FLOPs one launch of a kernel performs (per rank)."""
+    N, K, D = c["N"], c["K"], c["D"]
+    if name == "fwd_kernel":
+        return 2.0 * N * Vr * (K + D)
+    if name == "gemm_kernel":       # dh and dW of one chunk: 4 N C K per chunk, summed over the shard
+        return 4.0 * N * Vr * K / launches_per_step
+    if name == "bwd_scores_kernel":  # dP and dE (the S recompute is not algorithmic)
+        return 4.0 * N * Vr * D / launches_per_step
+    return None
+
+
+def cpu_reference_sample(c, vocab_rows, threads):
+    """The reference algorithm (numpy port of swvr's chunked path) fwd + bwd + MSE on a
+    vocabulary slice of the workload; returns seconds."""
+    from oracle import swvr_oracle as orc
+    rng = np.random.default_rng(0)
+    N, K, D = c["N"], c["K"], c["D"]
+    h = orc.round_bf16(rng.standard_normal((N, K), dtype=np.float32))
+    W = orc.round_bf16(K ** -0.5 * rng.standard_normal((vocab_rows, K), dtype=np.float32))
+    E = orc.round_bf16(0.02 * rng.standard_normal((vocab_rows, D), dtype=np.float32))
+    b = orc.round_bf16(0.02 * rng.standard_normal(vocab_rows, dtype=np.float32)) if c["bias"] else None
+    t = 0.02 * rng.standard_normal((N, D), dtype=np.float32)
+    w = (rng.random(N) < c["weight"]).astype(np.float32) if c["weight"] else None
+    t0 = time.perf_counter()
+    O, lse = orc.chunked_forward(h, W, E, b, 1.0, 8192, "bf16")
+    orc.mse_forward(O, lse, t, w, "mean", c["z"])
+    gO, glse, _, _ = orc.mse_backward(O, lse, t, w, "mean", c["z"])
+    orc.chunked_backward(gO, glse, h, W, E, b, O, lse, 1.0, 8192, "bf16")
+    return time.perf_counter() - t0
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def sized_cpu_sample(c, target_s):
+    """Grow the vocabulary slice until one fwd+bwd takes about target_s seconds."""
+    rows = 256
+    dt = cpu_reference_sample(c, rows, cpu_threads())
+    rows = int(min(c["V"], max(256, rows * target_s / max(dt, 1e-3))) // 256 * 256) or 256
+    return rows
+
+
+def run_reference_arm(args, c, rank, world):
+    """--impl reference: the reference's algorithm on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    rows = sized_cpu_sample(c, target_s=max(1.0, min(8.0, 150.0 / max(args.steps + args.warmup, 1))))
+    for _ in range(args.warmup):
+        cpu_reference_sample(c, rows, threads)
+    times = [cpu_reference_sample(c, rows, threads) for _ in range(args.steps)]
+    sec = sum(times) / len(times)
+    value = f_algo(c, rows) / sec / 1e12
+    sample = (f"vocabulary slice of {rows} of {c['V']} rows (N={c['N']}, K={c['K']}, D={c['D']}), bf16 values in "
+              f"fp32 numpy BLAS, chunk 8192, fwd+bwd+MSE; TFLOP/s scaled by the slice's F_algo")
+    line = {
+        "metric": "fwd+bwd TFLOP/s (algorithmic 6NV(K+D)) at N=16k,K=2560,V=152k,D=64",
+        "value": round(value, 4), "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3 * c["V"] / rows, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 inputs, fp32 math",
+        "data": "synthetic", "config": {"workload": f"{args.config} (vocabulary slice, see cpu_baseline.sample)",
+                                        "N": c["N"], "K": c["K"], "V": c["V"], "D": c["D"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--chunk", type=int, default=None, help="chunk_size (default: the API default, 8192)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    c = CONFIGS[args.config]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, c, rank, world)
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    r = run_ours(args, c, rank, world, device)
+
+    if rank == 0:
+        burst, sustained, peak_src = load_peaks()
+        F = f_algo(c)
+        value = F / (r["ms"] * 1e-3) / 1e12
+        launches = sum(v[0] for v in r["prof"].values())
+        per_step = {k: v[0] / args.steps for k, v in r["prof"].items()}
+        kernels = {}
+        for name, (n, tot) in r["prof"].items():
+            fl = kernel_flops(name, c, r["Vr"], per_step[name], args.chunk)
+            avg = tot / n
+            kernels[name] = {"launches": n, "avg_ms": round(avg, 4), "share": round(tot / max(1e-9, sum(
+                v[1] for v in r["prof"].values())), 4)}
+            if fl:
+                kernels[name]["algo_tflops"] = round(fl / (avg * 1e-3) / 1e12, 1)
+        dom = max(r["prof"].items(), key=lambda kv: kv[1][1])[0]
+        dom_fl = kernel_flops(dom, c, r["Vr"], per_step[dom], args.chunk)
+        dom_avg = r["prof"][dom][1] / r["prof"][dom][0]
+        achieved = dom_fl / (dom_avg * 1e-3) / 1e12 if dom_fl else None
+        line = {
+            "metric": "fwd+bwd TFLOP/s (algorithmic 6NV(K+D)) at N=16k,K=2560,V=152k,D=64",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(r["ms"], 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": {"workload": f"{args.config}: softmax_readout_mse fwd+bwd", "N": c["N"], "K": c["K"],
+                       "V": c["V"], "D": c["D"], "bias": c["bias"], "weight": c["weight"], "z_loss_weight": c["z"],
+                       "chunk_size": args.chunk or 8192, "parallelism": f"vocab-sharded x{world}" if world > 1
+                       else "single GPU", "l2": "inputs larger than L2 (W 778 MB); no flush"},
+            "tflops_exec": round((8.0 * c["N"] * c["V"] * c["K"] + 6.0 * c["N"] * c["V"] * c["D"]) /
+                                 (r["ms"] * 1e-3) / 1e12, 2),
+            "frac_of_peak": {"measured_burst": round(value / burst, 4), "measured_sustained": round(value / sustained, 4),
+                             "spec_2250": round(value / 2250.0, 4), "peak_source": peak_src},
+            "peak_mem_gib": round(r["peak_gib"], 3),
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1) if achieved else None,
+                         "peak": sustained, "unit": "TFLOP/s",
+                         "frac": round(achieved / sustained, 4) if achieved else None, "traffic": None,
+                         "peak_kind": f"{peak_src} sustained cuBLAS bf16 (kernel timed inside a long step)"},
+            "kernels": kernels,
+            "gpu_launches": launches,
+            "clocks": r["clocks"],
+            "e2e": {"value": round(F / (r["ms_e2e"] * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(r["ms_e2e"], 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = cpu_threads()
+            rows = sized_cpu_sample(c, target_s=10.0)
+            sec = cpu_reference_sample(c, rows, threads)
+            cv = f_algo(c, rows) / sec / 1e12
+            line["cpu_baseline"] = {"value": round(cv, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                    "sample": f"vocabulary slice of {rows} of {c['V']} rows, fwd+bwd+MSE, "
+                                              f"numpy port of swvr's chunked path; {sec:.1f} s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,191 @@
+/*
+ * swvr_b200 -- C ABI of the B200 (sm_100a) softmax-weighted embedding readout.
+ *
+ *   S   = logit_scale * h @ W^T + bias          h [N, K], W [V, K], bias [V]
+ *   O   = softmax(S) @ E,  LSE = logsumexp(S)   E [V, D], O [N, D], LSE [N]
+ *
+ * The [N, V] scores are never materialised.  This header is the boundary a host binds
+ * (ctypes / cgo / JNI / N-API): plain pointers, sizes and enums, no framework types.
+ *
+ * Conventions shared by every entry point
+ *   - All pointers are device pointers on the current CUDA device unless stated.
+ *   - `stream` is a cudaStream_t (may be NULL for the legacy default stream).  All work is
+ *     enqueued on it; nothing here synchronises the stream or the device.
+ *   - The library never allocates or frees device memory: callers pass every output and a
+ *     workspace of at least the size the matching *_workspace_size() call returns.
+ *   - Return value: SWVR_OK (0) or a negative SWVR_ERR_* code; swvr_last_error() then holds
+ *     a message (per host thread).  Errors raised by a bounded device-side wait surface on
+ *     the host through swvr_device_error().
+ *   - Reentrant: no call keeps state between calls except a per-device cache of kernel
+ *     attributes guarded by a mutex.
+ *   - Compute dtypes: SWVR_BF16 / SWVR_F16 run the tcgen05 tensor-core kernels (fp32
+ *     accumulation); SWVR_F32 / SWVR_F64 run exact SIMT CUDA kernels.  O, LSE and the
+ *     softmax state are fp64 for SWVR_F64 compute and fp32 otherwise (the accumulation dtype).
+ */
+#ifndef SWVR_B200_H
+#define SWVR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SWVR_ABI_VERSION 1
+
+enum swvr_status {
+  SWVR_OK = 0,
+  SWVR_ERR_INVALID_ARGUMENT = -1, /* bad shape / pointer / value: a ValueError in Python */
+  SWVR_ERR_UNSUPPORTED = -2,      /* a dtype, size or alignment the kernels do not cover */
+  SWVR_ERR_CUDA = -3,             /* a CUDA runtime / driver call or a launch failed */
+  SWVR_ERR_WORKSPACE = -4         /* the workspace passed is smaller than required */
+};
+
+enum swvr_dtype { SWVR_F32 = 0, SWVR_F64 = 1, SWVR_BF16 = 2, SWVR_F16 = 3 };
+
+enum swvr_reduction { SWVR_REDUCE_NONE = 0, SWVR_REDUCE_SUM = 1, SWVR_REDUCE_MEAN = 2 };
+
+/*
+ * One readout problem.  h, W and E share `compute_dtype`; rows may be padded (ld* is the
+ * row stride in elements, the last dimension is contiguous).  On the tensor-core path the
+ * base pointers must be 16-byte aligned and ld* * element size a multiple of 16 bytes.
+ * `chunk` is the number of vocabulary rows whose score gradients the backward stages at a
+ * time (the reference's chunk_size); the tensor-core path rounds it up to a multiple of 128.
+ */
+typedef struct swvr_problem {
+  int64_t n_tokens;   /* N  (rows of h)             */
+  int64_t hidden;     /* K                           */
+  int64_t vocab;      /* V  (rows of W, E, bias)     */
+  int64_t embed_dim;  /* D                           */
+  int32_t compute_dtype;
+  int32_t bias_dtype; /* ignored when bias == NULL   */
+  const void* h;
+  int64_t ldh;
+  const void* W;
+  int64_t ldw;
+  const void* E;
+  int64_t lde;
+  const void* bias;   /* [V] contiguous, or NULL     */
+  double logit_scale;
+  int64_t chunk;
+} swvr_problem;
+
+/*
+ * Forward.  Replaces the reference's custom op swvr::chunked_fwd
+ * (swvr/chunked.py:157-161 -> _forward, chunked.py:82-105): writes O [N, D] and LSE [N],
+ * contiguous, in the accumulation dtype.
+ */
+int swvr_fwd_workspace_size(const swvr_problem* p, size_t* bytes);
+int swvr_fwd(const swvr_problem* p, void* O, void* lse, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Forward of one vocabulary shard without the final normalisation: the online-softmax state
+ * of every row, m2 [N] (running maximum in log2 units, i.e. max of S * log2(e)),
+ * l [N] (sum of 2^(S*log2(e) - m2)) and acc [N, D] (sum of those weights times E rows),
+ * all in the accumulation dtype.  No counterpart in the reference (which has no vocabulary
+ * sharding); it is the per-chunk state of chunked.py:86-104 exposed across devices.
+ * Uses the same workspace size as swvr_fwd.
+ */
+int swvr_fwd_partial(const swvr_problem* p, void* m2, void* l, void* acc, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Merge `shards` partial states ([shards, N], [shards, N], [shards, N, D], shard-major,
+ * contiguous) in shard order into O [N, D] and LSE [N].  Deterministic.  The same merge as
+ * the chunk loop of chunked.py:96-105, applied across shards.
+ */
+int swvr_combine(int64_t shards, int64_t n_tokens, int64_t embed_dim, int32_t acc_dtype, const void* m2, const void* l,
+                 const void* acc, void* O, void* lse, void* stream);
+
+/*
+ * Backward inputs and outputs.  grad_O [N, D] and grad_lse [N] are contiguous in the
+ * accumulation dtype, as are the saved forward outputs O and lse.  A NULL grad_* pointer
+ * means "that input is frozen" (the reference's need_* flags, chunked.py:170-178); frozen
+ * inputs skip their GEMMs.  grad_W / grad_E rows may be padded (ld_* in elements).
+ * grad_h_acc, when not NULL, is an fp32 (fp64 for F64 compute) [N, K] buffer that receives
+ * the un-cast dh accumulator (a vocabulary shard's partial dh, summed across shards by the
+ * caller); grad_h may then be NULL.
+ */
+typedef struct swvr_grads {
+  const void* grad_O;
+  const void* grad_lse;
+  const void* O;
+  const void* lse;
+  void* grad_h;
+  int32_t grad_h_dtype;
+  void* grad_W;
+  int32_t grad_W_dtype;
+  int64_t ld_grad_W;
+  void* grad_E;
+  int32_t grad_E_dtype;
+  int64_t ld_grad_E;
+  void* grad_bias;
+  int32_t grad_bias_dtype;
+  void* grad_h_acc;
+} swvr_grads;
+
+/*
+ * Backward.  Replaces swvr::chunked_bwd (swvr/chunked.py:170-178 -> _backward, 108-151):
+ * recomputes the scores per vocabulary tile and writes dh, dW, dE and db.  dW, dE and db are
+ * deterministic (fixed-order reductions, no atomics); dh is accumulated in fp32 across
+ * chunks in chunk order.
+ */
+int swvr_bwd_workspace_size(const swvr_problem* p, const swvr_grads* g, size_t* bytes);
+int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * MSE / z-loss / per-token-weight epilogue, forward.  Replaces the loss arithmetic of
+ * softmax_readout_mse (swvr/api.py:54-66):
+ *   per_tok = mean_d (O - target)^2 + z_loss_weight * LSE^2, times weight[n] if weight;
+ *   NONE -> out [N]; SUM -> out [1] = sum; MEAN -> out [1] = sum / (sum(weight) or N).
+ * O, lse, target, weight (may be NULL), out and stats share `dtype` (F32 or F64).  For SUM and
+ * MEAN one CUDA block reduces in a fixed order (deterministic) and, when stats is not NULL,
+ * writes stats[0] = sum_n weight[n] * per_tok[n] and stats[1] = the denominator (1 for SUM).
+ */
+int swvr_mse_fwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,
+                 const void* target, const void* weight, double z_loss_weight, int32_t reduction, void* out,
+                 void* stats, void* stream);
+
+/*
+ * Gradient of swvr_mse_fwd for upstream grad_out ([1] for SUM/MEAN, [N] for NONE): writes
+ * grad_O [N, D], grad_lse [N] and, when not NULL, grad_target [N, D] and grad_weight [N].
+ * `stats` is the array swvr_mse_fwd wrote (required for MEAN, ignored otherwise).
+ */
+int swvr_mse_bwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,
+                 const void* target, const void* weight, double z_loss_weight, int32_t reduction,
+                 const void* grad_out, const void* stats, void* grad_O, void* grad_lse, void* grad_target,
+                 void* grad_weight, void* stream);
+
+/*
+ * Launch accounting for benchmarks (no counterpart in the reference).  Between
+ * swvr_profile_start() and swvr_profile_stop(), every kernel the library launches from any
+ * host thread is counted per kind and bracketed by a pair of CUDA events on its stream.
+ * swvr_profile_stop() waits for those events and fills up to max_records records (one per
+ * kernel kind that ran): launches and summed event time in milliseconds.
+ */
+typedef struct swvr_profile_record {
+  char name[32];
+  int64_t launches;
+  double total_ms;
+} swvr_profile_record;
+
+int swvr_profile_start(void);
+int swvr_profile_stop(swvr_profile_record* records, int max_records, int* n_records);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* swvr_last_error(void);
+
+/*
+ * Read and clear the device error word of the current device: *code = 0 when no bounded
+ * device-side wait has expired since the last call.  Synchronises with the device.
+ */
+int swvr_device_error(uint32_t* code);
+
+int swvr_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWVR_B200_H */

@@ -1,0 +1,589 @@
+// extern "C" entry points of libswvr_b200.so (declared in include/swvr_b200.h): argument
+// validation, work planning, TMA descriptor construction and the backward chunk loop.
+// No device memory is allocated here; callers pass outputs and workspaces.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "simt.cuh"
+#include "small.cuh"
+#include "tc.cuh"
+
+namespace swvr {
+
+static thread_local std::string t_err;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+#define SWVR_CUDA(call)                                                                            \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return fail(SWVR_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define SWVR_TRY(call)          \
+  do {                          \
+    int rc_ = (call);           \
+    if (rc_ != SWVR_OK) return rc_; \
+  } while (0)
+
+static int num_sms() {
+  int dev = 0, n = kNumSMsB200;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kNumSMsB200;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kNumSMsB200;
+  return n > 0 ? n : kNumSMsB200;
+}
+
+
+// ---------------------------------------------------------------------------- launch accounting
+enum ProfKind { kProfFwd = 0, kProfBwdScores, kProfGemm, kProfCombine, kProfReduce, kProfPrologue, kProfCast,
+                kProfMse, kProfSimt, kProfKinds };
+static const char* kProfNames[kProfKinds] = {"fwd_kernel",      "bwd_scores_kernel", "gemm_kernel",
+                                             "combine_kernel",  "reduce_de_db_kernel", "prologue_kernel",
+                                             "cast_kernel",     "mse_kernel",        "simt_kernels"};
+static std::mutex g_prof_mu;
+static bool g_prof_on = false;
+static int64_t g_prof_launches[kProfKinds];
+struct ProfPending {
+  int kind;
+  cudaEvent_t e0, e1;
+};
+static std::vector<ProfPending> g_prof_pending;
+static std::vector<cudaEvent_t> g_prof_pool;
+
+static cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets one kernel launch (or a group, `count` launches) with events when profiling.
+struct ProfScope {
+  int kind;
+  int64_t count;
+  cudaStream_t st;
+  cudaEvent_t e0 = nullptr;
+  ProfScope(int k, cudaStream_t s, int64_t n = 1) : kind(k), count(n), st(s) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on) return;
+    e0 = prof_event();
+    if (e0) cudaEventRecord(e0, st);
+  }
+  ~ProfScope() {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on || !e0) return;
+    cudaEvent_t e1 = prof_event();
+    if (!e1) return;
+    cudaEventRecord(e1, st);
+    g_prof_launches[kind] += count;
+    g_prof_pending.push_back({kind, e0, e1});
+  }
+};
+
+static bool is_tc(int dt) { return dt == SWVR_BF16 || dt == SWVR_F16; }
+static int acc_dtype_of(int cdt) { return cdt == SWVR_F64 ? SWVR_F64 : SWVR_F32; }
+
+// ---------------------------------------------------------------------------- TMA descriptors
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with a row pitch of row_bytes; 128-byte swizzle, zero
+// fill out of bounds.
+static int make_map(CUtensorMap* m, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+  EncodeFn fn = encode_fn();
+  if (!fn) return fail(SWVR_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_bytes & 15u) != 0)
+    return fail(SWVR_ERR_UNSUPPORTED, "TMA operand not 16-byte aligned (base %p, row pitch %llu bytes)", base,
+                static_cast<unsigned long long>(row_bytes));
+  const CUtensorMapDataType t = dt == SWVR_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : dt == SWVR_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[2] = {inner > 0 ? inner : 1, outer > 0 ? outer : 1};
+  cuuint64_t strides[1] = {row_bytes > 0 ? row_bytes : 16};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(m, t, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SWVR_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (%d): dims {%llu, %llu}, pitch %llu, box {%u, %u}",
+                static_cast<int>(r), static_cast<unsigned long long>(inner), static_cast<unsigned long long>(outer),
+                static_cast<unsigned long long>(row_bytes), box_inner, box_outer);
+  return SWVR_OK;
+}
+
+// ---------------------------------------------------------------------------- validation
+static int validate(const swvr_problem* p) {
+  if (!p) return fail(SWVR_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (p->n_tokens < 0 || p->hidden < 0 || p->vocab < 0 || p->embed_dim < 0)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "negative size");
+  if (p->n_tokens >= (1ll << 31) || p->vocab >= (1ll << 31) || p->hidden >= (1ll << 31) || p->embed_dim >= (1ll << 31))
+    return fail(SWVR_ERR_UNSUPPORTED, "sizes must be below 2^31");
+  if (p->compute_dtype < SWVR_F32 || p->compute_dtype > SWVR_F16)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown compute dtype %d", p->compute_dtype);
+  if (p->bias && (p->bias_dtype < SWVR_F32 || p->bias_dtype > SWVR_F16))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown bias dtype %d", p->bias_dtype);
+  if (p->chunk <= 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "chunk must be positive, got %lld", (long long)p->chunk);
+  if (p->ldh < p->hidden || p->ldw < p->hidden || p->lde < p->embed_dim)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "row stride smaller than the row length");
+  if ((p->n_tokens > 0 && p->hidden > 0 && !p->h) || (p->vocab > 0 && p->hidden > 0 && !p->W) ||
+      (p->vocab > 0 && p->embed_dim > 0 && !p->E))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL input pointer");
+  if (is_tc(p->compute_dtype)) {
+    if (p->embed_dim < 1 || p->embed_dim > 128)
+      return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path supports 1 <= D <= 128, got %lld", (long long)p->embed_dim);
+    if (p->hidden < 8 || (p->hidden % 8) != 0 || (p->ldh % 8) != 0 || (p->ldw % 8) != 0 || (p->lde % 8) != 0)
+      return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path needs K and row strides that are multiples of 8 elements");
+    if ((reinterpret_cast<uintptr_t>(p->h) | reinterpret_cast<uintptr_t>(p->W) | reinterpret_cast<uintptr_t>(p->E)) & 15u)
+      return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned h, W and E");
+  }
+  return SWVR_OK;
+}
+
+// ---------------------------------------------------------------------------- forward plan
+struct FwdPlan {
+  int DP, BV, MT, VT, splits, per, units, grid;
+  size_t off_m2, off_l, off_acc, bytes;
+};
+
+static FwdPlan plan_fwd(const swvr_problem& p) {
+  FwdPlan f{};
+  const int sms = num_sms();
+  f.DP = p.embed_dim <= 64 ? 64 : 128;
+  f.BV = tc::fwd_vocab_tile(f.DP);
+  f.MT = static_cast<int>(ceil_div(p.n_tokens, 128));
+  f.VT = static_cast<int>(ceil_div(p.vocab, f.BV));
+  int best_s = 1;
+  int64_t best_cost = -1;
+  const int smax = std::max(1, std::min(f.VT, 64));
+  for (int s = 1; s <= smax; ++s) {
+    const int64_t cost = ceil_div(static_cast<int64_t>(f.MT) * s, sms) * ceil_div(f.VT, s);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_s = s;
+    }
+  }
+  f.per = static_cast<int>(ceil_div(std::max(f.VT, 1), best_s));
+  f.splits = static_cast<int>(ceil_div(std::max(f.VT, 1), f.per));
+  f.units = f.MT * f.splits;
+  f.grid = std::max(1, std::min(f.units, sms));
+  const size_t rows = static_cast<size_t>(f.units) * 128;
+  f.off_m2 = 0;
+  f.off_l = align_up(rows * 4, 256);
+  f.off_acc = f.off_l + align_up(rows * 4, 256);
+  f.bytes = f.off_acc + align_up(rows * p.embed_dim * 4, 256) + 256;
+  return f;
+}
+
+static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo, void* acco, void* ws, size_t wsb,
+                  cudaStream_t st) {
+  const FwdPlan f = plan_fwd(p);
+  if (wsb < f.bytes) return fail(SWVR_ERR_WORKSPACE, "forward workspace %zu < required %zu", wsb, f.bytes);
+  if (p.n_tokens == 0) return SWVR_OK;
+  const bool bf16 = p.compute_dtype == SWVR_BF16;
+  tc::FwdMaps maps;
+  SWVR_TRY(make_map(&maps.h, p.h, p.compute_dtype, p.hidden, p.n_tokens, p.ldh * 2, 64, 128));
+  SWVR_TRY(make_map(&maps.w, p.W, p.compute_dtype, p.hidden, p.vocab, p.ldw * 2, 64, f.BV));
+  SWVR_TRY(make_map(&maps.e, p.E, p.compute_dtype, p.embed_dim, p.vocab, p.lde * 2, 64, f.BV));
+  char* w = static_cast<char*>(ws);
+  tc::FwdParams prm{};
+  prm.N = static_cast<int>(p.n_tokens);
+  prm.K = static_cast<int>(p.hidden);
+  prm.V = static_cast<int>(p.vocab);
+  prm.D = static_cast<int>(p.embed_dim);
+  prm.sc2 = static_cast<float>(p.logit_scale * 1.4426950408889634);
+  prm.bias = p.bias;
+  prm.bias_dt = p.bias_dtype;
+  prm.MT = f.MT;
+  prm.VT = f.VT;
+  prm.splits = f.splits;
+  prm.per = f.per;
+  prm.units = f.units;
+  prm.part_m2 = reinterpret_cast<float*>(w + f.off_m2);
+  prm.part_l = reinterpret_cast<float*>(w + f.off_l);
+  prm.part_acc = reinterpret_cast<float*>(w + f.off_acc);
+  if (p.vocab == 0) return fail(SWVR_ERR_UNSUPPORTED, "empty vocabulary (callers handle V == 0)");
+  {
+    ProfScope ps(kProfFwd, st);
+    SWVR_CUDA(tc::launch_fwd_kernel(bf16, f.DP, maps, prm, f.grid, st));
+  }
+  ProfScope ps_c(kProfCombine, st);
+  SWVR_CUDA(small::combine(SWVR_F32, f.splits, p.n_tokens, p.embed_dim, prm.part_m2, prm.part_l, prm.part_acc, 0,
+                           f.splits, O, lse, m2o, lo, acco, st));
+  return SWVR_OK;
+}
+
+// ---------------------------------------------------------------------------- backward plan
+static void choose_ts(int VTc, int NT, int sms, int* TS, int* per_t) {
+  int best = 1;
+  int64_t best_cost = -1;
+  const int tmax = std::max(1, std::min(NT, 32));
+  for (int ts = 1; ts <= tmax; ++ts) {
+    const int64_t cost = ceil_div(static_cast<int64_t>(VTc) * ts, sms) * ceil_div(NT, ts);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = ts;
+    }
+  }
+  *per_t = static_cast<int>(ceil_div(std::max(NT, 1), best));
+  *TS = static_cast<int>(ceil_div(std::max(NT, 1), *per_t));
+}
+
+struct BwdPlan {
+  int DP, NT, C, sms;
+  int64_t Npad;
+  bool need_h, need_W, need_E, need_b, need_ds;
+  size_t off_delta, off_goc, off_ds, off_dh, off_de, off_db, bytes;
+  int max_units;
+};
+
+static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
+  BwdPlan b{};
+  b.sms = num_sms();
+  b.DP = p.embed_dim <= 64 ? 64 : 128;
+  b.NT = static_cast<int>(ceil_div(p.n_tokens, 128));
+  b.Npad = static_cast<int64_t>(b.NT) * 128;
+  int64_t C = round_up(std::max<int64_t>(p.chunk, 1), 128);
+  C = std::min<int64_t>(C, round_up(std::max<int64_t>(p.vocab, 1), 128));
+  b.C = static_cast<int>(C);
+  b.need_h = g.grad_h || g.grad_h_acc;
+  b.need_W = g.grad_W != nullptr;
+  b.need_E = g.grad_E != nullptr;
+  b.need_b = g.grad_bias != nullptr && p.bias != nullptr;
+  b.need_ds = b.need_h || b.need_W;
+  // the largest units count over the full chunk and the tail chunk
+  b.max_units = 1;
+  for (int64_t rows : {C, p.vocab % C}) {
+    if (rows <= 0) continue;
+    const int VTc = static_cast<int>(ceil_div(rows, 128));
+    int TS, per_t;
+    choose_ts(VTc, b.NT, b.sms, &TS, &per_t);
+    b.max_units = std::max(b.max_units, VTc * TS);
+  }
+  size_t off = 0;
+  b.off_delta = off;
+  off += align_up(static_cast<size_t>(b.Npad) * 4, 256);
+  b.off_goc = off;
+  off += align_up(static_cast<size_t>(b.Npad) * b.DP * 2, 256);
+  b.off_ds = off;
+  if (b.need_ds) off += align_up(static_cast<size_t>(C) * b.Npad * 2, 256);
+  b.off_dh = off;
+  if (b.need_h && !g.grad_h_acc) off += align_up(static_cast<size_t>(p.n_tokens) * p.hidden * 4, 256);
+  b.off_de = off;
+  if (b.need_E) off += align_up(static_cast<size_t>(b.max_units) * 128 * p.embed_dim * 4, 256);
+  b.off_db = off;
+  if (b.need_b) off += align_up(static_cast<size_t>(b.max_units) * 128 * 4, 256);
+  b.bytes = off + 256;
+  return b;
+}
+
+static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t wsb, cudaStream_t st) {
+  const BwdPlan b = plan_bwd(p, g);
+  if (wsb < b.bytes) return fail(SWVR_ERR_WORKSPACE, "backward workspace %zu < required %zu", wsb, b.bytes);
+  const int64_t N = p.n_tokens, K = p.hidden, V = p.vocab, D = p.embed_dim;
+  if (g.grad_W && !(g.grad_W_dtype == p.compute_dtype || g.grad_W_dtype == SWVR_F32))
+    return fail(SWVR_ERR_UNSUPPORTED, "grad_W must be in the compute dtype or fp32");
+  if (g.grad_W && ((reinterpret_cast<uintptr_t>(g.grad_W) & 15u) || (g.ld_grad_W * dtype_size(g.grad_W_dtype)) % 16))
+    return fail(SWVR_ERR_UNSUPPORTED, "grad_W must be 16-byte aligned with a 16-byte multiple row pitch");
+  if (N == 0 || V == 0) {
+    if (g.grad_W) SWVR_CUDA(small::zero_rows(g.grad_W, g.grad_W_dtype, V, K, g.ld_grad_W, st));
+    if (g.grad_E) SWVR_CUDA(small::zero_rows(g.grad_E, g.grad_E_dtype, V, D, g.ld_grad_E, st));
+    if (g.grad_bias) SWVR_CUDA(small::zero_rows(g.grad_bias, g.grad_bias_dtype, 1, V, V, st));
+    if (g.grad_h) SWVR_CUDA(small::zero_rows(g.grad_h, g.grad_h_dtype, N, K, K, st));
+    if (g.grad_h_acc) SWVR_CUDA(cudaMemsetAsync(g.grad_h_acc, 0, static_cast<size_t>(N) * K * 4, st));
+    return SWVR_OK;
+  }
+  const bool bf16 = p.compute_dtype == SWVR_BF16;
+  char* w = static_cast<char*>(ws);
+  float* delta = reinterpret_cast<float*>(w + b.off_delta);
+  void* goc = w + b.off_goc;
+  void* ds = b.need_ds ? static_cast<void*>(w + b.off_ds) : nullptr;
+  float* dh = b.need_h ? (g.grad_h_acc ? static_cast<float*>(g.grad_h_acc) : reinterpret_cast<float*>(w + b.off_dh))
+                       : nullptr;
+  float* part_de = b.need_E ? reinterpret_cast<float*>(w + b.off_de) : nullptr;
+  float* part_db = b.need_b ? reinterpret_cast<float*>(w + b.off_db) : nullptr;
+
+  {
+  ProfScope ps(kProfPrologue, st);
+  SWVR_CUDA(small::prologue(bf16, static_cast<const float*>(g.O), static_cast<const float*>(g.grad_O),
+                            static_cast<const float*>(g.grad_lse), N, static_cast<int>(D), b.DP, delta, goc, st));
+  }
+  if (dh) SWVR_CUDA(cudaMemsetAsync(dh, 0, static_cast<size_t>(N) * K * 4, st));
+
+  tc::BwdScoresMaps sm;
+  SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.h, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.e, p.E, p.compute_dtype, D, V, p.lde * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.go, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 128));
+  tc::GemmMaps gm;
+  if (b.need_ds) {
+    SWVR_TRY(make_map(&gm.h_mn, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
+    SWVR_TRY(make_map(&gm.w_mn, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 64));
+    if (g.grad_W) {
+      if (g.grad_W_dtype == SWVR_F32)
+        SWVR_TRY(make_map(&gm.gw, g.grad_W, SWVR_F32, K, V, g.ld_grad_W * 4, 32, 128));
+      else
+        SWVR_TRY(make_map(&gm.gw, g.grad_W, p.compute_dtype, K, V, g.ld_grad_W * 2, 64, 128));
+    } else {
+      gm.gw = gm.w_mn;  // unused
+    }
+    if (dh)
+      SWVR_TRY(make_map(&gm.dh, dh, SWVR_F32, K, N, K * 4, 32, 128));
+    else
+      gm.dh = gm.w_mn;  // unused
+  }
+
+  for (int64_t v0 = 0; v0 < V; v0 += b.C) {
+    const int64_t v1 = std::min<int64_t>(v0 + b.C, V);
+    const int rows = static_cast<int>(v1 - v0);
+    const int VTc = static_cast<int>(ceil_div(rows, 128));
+    int TS, per_t;
+    choose_ts(VTc, b.NT, b.sms, &TS, &per_t);
+    tc::BwdScoresParams sp{};
+    sp.N = static_cast<int>(N);
+    sp.K = static_cast<int>(K);
+    sp.D = static_cast<int>(D);
+    sp.v_begin = static_cast<int>(v0);
+    sp.v_end = static_cast<int>(v1);
+    sp.scale = static_cast<float>(p.logit_scale);
+    sp.sc2 = static_cast<float>(p.logit_scale * 1.4426950408889634);
+    sp.bias = p.bias;
+    sp.bias_dt = p.bias_dtype;
+    sp.lse = static_cast<const float*>(g.lse);
+    sp.delta = delta;
+    sp.NT = b.NT;
+    sp.VT = VTc;
+    sp.TS = TS;
+    sp.per_t = per_t;
+    sp.units = VTc * TS;
+    sp.ds = ds;
+    sp.ld_ds = b.Npad;
+    sp.part_de = part_de;
+    sp.part_db = part_db;
+    {
+      ProfScope ps(kProfBwdScores, st);
+      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, std::min(sp.units, b.sms), st));
+    }
+    if (part_de || part_db) {
+      void* gE = g.grad_E;
+      ProfScope ps(kProfReduce, st);
+      SWVR_CUDA(small::reduce_de_db(part_de, part_db, TS, per_t, b.NT, static_cast<int>(v0), rows, D, gE,
+                                    g.grad_E_dtype, g.ld_grad_E, g.grad_bias, g.grad_bias_dtype, st));
+    }
+    if (b.need_ds) {
+      SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
+      SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
+      tc::GemmParams gp{};
+      const int nt = static_cast<int>(ceil_div(K, 256));
+      gp.dw_mt = VTc;
+      gp.dw_nt = nt;
+      gp.dw_kb = static_cast<int>(b.Npad / 64);
+      gp.dw_tiles = g.grad_W ? VTc * nt : 0;
+      gp.dh_mt = b.NT;
+      gp.dh_nt = nt;
+      gp.dh_kb = static_cast<int>(ceil_div(rows, 64));
+      gp.dh_tiles = dh ? b.NT * nt : 0;
+      gp.v_begin = static_cast<int>(v0);
+      gp.gw_f32 = g.grad_W_dtype == SWVR_F32 ? 1 : 0;
+      const int tiles = gp.dw_tiles + gp.dh_tiles;
+      if (tiles > 0) {
+        ProfScope ps(kProfGemm, st);
+        SWVR_CUDA(tc::launch_gemm_kernel(bf16, gm, gp, std::min(tiles, b.sms), st));
+      }
+    }
+  }
+  if (g.grad_h) {
+    ProfScope ps(kProfCast, st);
+    SWVR_CUDA(small::cast_f32(dh, g.grad_h, g.grad_h_dtype, N * K, st));
+  }
+  return SWVR_OK;
+}
+
+}  // namespace swvr
+
+// ================================================================================ extern "C"
+using namespace swvr;
+
+extern "C" {
+
+int swvr_abi_version(void) { return SWVR_ABI_VERSION; }
+
+const char* swvr_last_error(void) { return t_err.c_str(); }
+
+int swvr_device_error(uint32_t* code) {
+  if (!code) return fail(SWVR_ERR_INVALID_ARGUMENT, "code is NULL");
+  unsigned int v = 0, zero = 0;
+  SWVR_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)));
+  SWVR_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+  *code = v;
+  return SWVR_OK;
+}
+
+int swvr_profile_start(void) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& pe : g_prof_pending) {
+    g_prof_pool.push_back(pe.e0);
+    g_prof_pool.push_back(pe.e1);
+  }
+  g_prof_pending.clear();
+  for (int k = 0; k < kProfKinds; ++k) g_prof_launches[k] = 0;
+  g_prof_on = true;
+  return SWVR_OK;
+}
+
+int swvr_profile_stop(swvr_profile_record* records, int max_records, int* n_records) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_on = false;
+  double ms[kProfKinds] = {0};
+  for (auto& pe : g_prof_pending) {
+    float t = 0.f;
+    if (cudaEventSynchronize(pe.e1) != cudaSuccess) return fail(SWVR_ERR_CUDA, "profile event wait failed");
+    if (cudaEventElapsedTime(&t, pe.e0, pe.e1) == cudaSuccess) ms[pe.kind] += t;
+    g_prof_pool.push_back(pe.e0);
+    g_prof_pool.push_back(pe.e1);
+  }
+  g_prof_pending.clear();
+  int n = 0;
+  for (int k = 0; k < kProfKinds; ++k) {
+    if (g_prof_launches[k] == 0) continue;
+    if (records && n < max_records) {
+      std::memset(records[n].name, 0, sizeof(records[n].name));
+      std::strncpy(records[n].name, kProfNames[k], sizeof(records[n].name) - 1);
+      records[n].launches = g_prof_launches[k];
+      records[n].total_ms = ms[k];
+    }
+    ++n;
+  }
+  if (n_records) *n_records = n;
+  return SWVR_OK;
+}
+
+int swvr_fwd_workspace_size(const swvr_problem* p, size_t* bytes) {
+  SWVR_TRY(validate(p));
+  if (!bytes) return fail(SWVR_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  *bytes = is_tc(p->compute_dtype) ? plan_fwd(*p).bytes : simt::fwd_workspace(*p);
+  return SWVR_OK;
+}
+
+int swvr_fwd(const swvr_problem* p, void* O, void* lse, void* ws, size_t wsb, void* stream) {
+  SWVR_TRY(validate(p));
+  if (p->n_tokens > 0 && (!O || !lse)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (is_tc(p->compute_dtype)) return tc_fwd(*p, O, lse, nullptr, nullptr, nullptr, ws, wsb, st);
+  if (wsb < simt::fwd_workspace(*p)) return fail(SWVR_ERR_WORKSPACE, "forward workspace too small");
+  ProfScope ps(kProfSimt, st);
+  return simt::fwd(*p, O, lse, nullptr, nullptr, nullptr, ws, st) == SWVR_OK
+             ? SWVR_OK
+             : fail(SWVR_ERR_CUDA, "SIMT forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+}
+
+int swvr_fwd_partial(const swvr_problem* p, void* m2, void* l, void* acc, void* ws, size_t wsb, void* stream) {
+  SWVR_TRY(validate(p));
+  if (p->n_tokens > 0 && (!m2 || !l || !acc)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (is_tc(p->compute_dtype)) return tc_fwd(*p, nullptr, nullptr, m2, l, acc, ws, wsb, st);
+  if (wsb < simt::fwd_workspace(*p)) return fail(SWVR_ERR_WORKSPACE, "forward workspace too small");
+  ProfScope ps(kProfSimt, st);
+  return simt::fwd(*p, nullptr, nullptr, m2, l, acc, ws, st) == SWVR_OK
+             ? SWVR_OK
+             : fail(SWVR_ERR_CUDA, "SIMT forward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+}
+
+int swvr_combine(int64_t shards, int64_t n_tokens, int64_t embed_dim, int32_t acc_dt, const void* m2, const void* l,
+                 const void* acc, void* O, void* lse, void* stream) {
+  if (shards <= 0 || n_tokens < 0 || embed_dim < 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "bad combine sizes");
+  if (acc_dt != SWVR_F32 && acc_dt != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "combine dtype must be F32/F64");
+  if (n_tokens > 0 && (!m2 || !l || !acc || !O || !lse)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  ProfScope ps(kProfCombine, static_cast<cudaStream_t>(stream));
+  SWVR_CUDA(small::combine(acc_dt, static_cast<int>(shards), n_tokens, embed_dim, m2, l, acc, 1, 1, O, lse, nullptr,
+                           nullptr, nullptr, static_cast<cudaStream_t>(stream)));
+  return SWVR_OK;
+}
+
+int swvr_bwd_workspace_size(const swvr_problem* p, const swvr_grads* g, size_t* bytes) {
+  SWVR_TRY(validate(p));
+  if (!g || !bytes) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL argument");
+  *bytes = is_tc(p->compute_dtype) ? plan_bwd(*p, *g).bytes : simt::bwd_workspace(*p, *g);
+  return SWVR_OK;
+}
+
+int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* ws, size_t wsb, void* stream) {
+  SWVR_TRY(validate(p));
+  if (!g) return fail(SWVR_ERR_INVALID_ARGUMENT, "grads is NULL");
+  if (p->n_tokens > 0 && (!g->grad_O || !g->grad_lse || !g->O || !g->lse))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL backward input");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (is_tc(p->compute_dtype)) return tc_bwd(*p, *g, ws, wsb, st);
+  if (wsb < simt::bwd_workspace(*p, *g)) return fail(SWVR_ERR_WORKSPACE, "backward workspace too small");
+  ProfScope ps(kProfSimt, st);
+  return simt::bwd(*p, *g, ws, st) == SWVR_OK
+             ? SWVR_OK
+             : fail(SWVR_ERR_CUDA, "SIMT backward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+}
+
+int swvr_mse_fwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,
+                 const void* target, const void* weight, double z, int32_t reduction, void* out, void* stats,
+                 void* stream) {
+  if (n_tokens < 0 || embed_dim < 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "negative size");
+  if (dtype != SWVR_F32 && dtype != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "loss dtype must be F32/F64");
+  if (reduction < SWVR_REDUCE_NONE || reduction > SWVR_REDUCE_MEAN)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown reduction %d", reduction);
+  if (!out || (n_tokens > 0 && (!O || !lse || !target))) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  ProfScope ps(kProfMse, static_cast<cudaStream_t>(stream));
+  SWVR_CUDA(small::mse_fwd(dtype, n_tokens, embed_dim, O, lse, target, weight, z, reduction, out, stats,
+                           static_cast<cudaStream_t>(stream)));
+  return SWVR_OK;
+}
+
+int swvr_mse_bwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,
+                 const void* target, const void* weight, double z, int32_t reduction, const void* grad_out,
+                 const void* stats, void* grad_O, void* grad_lse, void* grad_target, void* grad_weight,
+                 void* stream) {
+  if (n_tokens < 0 || embed_dim < 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "negative size");
+  if (dtype != SWVR_F32 && dtype != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "loss dtype must be F32/F64");
+  if (reduction < SWVR_REDUCE_NONE || reduction > SWVR_REDUCE_MEAN)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown reduction %d", reduction);
+  if (reduction == SWVR_REDUCE_MEAN && !stats) return fail(SWVR_ERR_INVALID_ARGUMENT, "MEAN needs stats");
+  if (n_tokens > 0 && (!O || !lse || !target || !grad_out || !grad_O || !grad_lse))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  ProfScope ps(kProfMse, static_cast<cudaStream_t>(stream));
+  SWVR_CUDA(small::mse_bwd(dtype, n_tokens, embed_dim, O, lse, target, weight, z, reduction, grad_out, stats, grad_O,
+                           grad_lse, grad_target, grad_weight, static_cast<cudaStream_t>(stream)));
+  return SWVR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,288 @@
+// Small memory-bound kernels around the tensor-core kernels: the online-softmax combine,
+// the deterministic dE / db reduction, the backward prologue, the MSE / z-loss epilogue
+// and dtype casts.
+#include <cmath>
+
+#include "common.cuh"
+#include "small.cuh"
+
+namespace swvr {
+namespace small {
+
+// ------------------------------------------------------------------ combine
+// Source s of row n lives at idx(s, n): split slots of the tensor-core forward
+// (mode 0: ((n/128)*splits + s)*128 + n%128) or shard-major arrays (mode 1: s*N + n).
+template <typename T>
+__global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict__ m2, const T* __restrict__ l,
+                               const T* __restrict__ acc, int mode, int splits, T* O, T* lse, T* m2o, T* lo, T* acco) {
+  const int64_t n = blockIdx.x;
+  auto idx = [&](int s) -> int64_t {
+    return mode == 0 ? ((n / 128) * splits + s) * 128 + (n % 128) : static_cast<int64_t>(s) * N + n;
+  };
+  double M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmax(M, static_cast<double>(m2[idx(s)]));
+  const double ref = isinf(M) ? 0.0 : M;
+  double L = 0.0;
+  for (int s = 0; s < S; ++s) {
+    const double w = exp2(static_cast<double>(m2[idx(s)]) - ref);
+    L += w == 0.0 ? 0.0 : static_cast<double>(l[idx(s)]) * w;
+  }
+  for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+    double A = 0.0;
+    for (int s = 0; s < S; ++s) {
+      const double w = exp2(static_cast<double>(m2[idx(s)]) - ref);
+      A += w == 0.0 ? 0.0 : static_cast<double>(acc[idx(s) * D + d]) * w;
+    }
+    if (O) O[n * D + d] = static_cast<T>(A / L);
+    if (acco) acco[n * D + d] = static_cast<T>(A);
+  }
+  if (threadIdx.x == 0) {
+    if (lse) lse[n] = static_cast<T>((ref + log2(L)) * 0.6931471805599453);
+    if (m2o) m2o[n] = static_cast<T>(M);
+    if (lo) lo[n] = static_cast<T>(L);
+  }
+}
+
+cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
+                    int splits, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
+  if (acc_dt == SWVR_F64)
+    combine_kernel<double><<<static_cast<unsigned>(N), threads, 0, st>>>(
+        S, N, D, static_cast<const double*>(m2), static_cast<const double*>(l), static_cast<const double*>(acc), mode,
+        splits, static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
+        static_cast<double*>(lo), static_cast<double*>(acco));
+  else
+    combine_kernel<float><<<static_cast<unsigned>(N), threads, 0, st>>>(
+        S, N, D, static_cast<const float*>(m2), static_cast<const float*>(l), static_cast<const float*>(acc), mode,
+        splits, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o), static_cast<float*>(lo),
+        static_cast<float*>(acco));
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ dE / db reduction
+// Row v of the chunk: sum its TS token-split partial slots in split order.
+__global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const float* __restrict__ part_db, int TS,
+                                    int per_t, int NT, int v_begin, int64_t D, void* gE, int gE_dt, int64_t ld_gE,
+                                    void* gb, int gb_dt) {
+  const int rr = blockIdx.x;  // row within the chunk
+  const int vt = rr / 128, r = rr % 128;
+  const int64_t v = v_begin + rr;
+  if (part_de) {
+    for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+      float s = 0.f;
+      for (int ts = 0; ts < TS; ++ts) {
+        if (ts * per_t >= NT) break;
+        s += part_de[((static_cast<int64_t>(vt) * TS + ts) * 128 + r) * D + d];
+      }
+      store_f(gE, gE_dt, v * ld_gE + d, s);
+    }
+  }
+  if (part_db && threadIdx.x == 0) {
+    float s = 0.f;
+    for (int ts = 0; ts < TS; ++ts) {
+      if (ts * per_t >= NT) break;
+      s += part_db[(static_cast<int64_t>(vt) * TS + ts) * 128 + r];
+    }
+    store_f(gb, gb_dt, v, s);
+  }
+}
+
+cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
+                         int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  reduce_de_db_kernel<<<rows, D >= 128 ? 128 : 64, 0, st>>>(part_de, part_db, TS, per_t, NT, v_begin, D, gE, gE_dt,
+                                                             ld_gE, gb, gb_dt);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ backward prologue
+// delta = rowsum(O * gO) - glse (swvr/chunked.py:112-113) and gO rounded to the compute
+// dtype, zero-padded to DP columns (chunked.py:114).  One warp per row.
+template <bool kBF16>
+__global__ void prologue_kernel(const float* __restrict__ O, const float* __restrict__ gO,
+                                const float* __restrict__ glse, int64_t N, int D, int DP, float* delta, void* gOc) {
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int d = lane; d < DP; d += 32) {
+    const float go = d < D ? gO[n * D + d] : 0.f;
+    if (d < D) s += O[n * D + d] * go;
+    if constexpr (kBF16)
+      static_cast<__nv_bfloat16*>(gOc)[n * DP + d] = __float2bfloat16_rn(go);
+    else
+      static_cast<__half*>(gOc)[n * DP + d] = __float2half_rn(go);
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) delta[n] = s - glse[n];
+}
+
+cudaError_t prologue(bool bf16, const float* O, const float* gO, const float* glse, int64_t N, int D, int DP,
+                     float* delta, void* gOc, cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>(ceil_div(N, 8));
+  if (bf16)
+    prologue_kernel<true><<<blocks, 256, 0, st>>>(O, gO, glse, N, D, DP, delta, gOc);
+  else
+    prologue_kernel<false><<<blocks, 256, 0, st>>>(O, gO, glse, N, D, DP, delta, gOc);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ casts
+__global__ void cast_f32_kernel(const float* __restrict__ src, void* dst, int dt, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    store_f(dst, dt, i, src[i]);
+}
+
+cudaError_t cast_f32(const float* src, void* dst, int dt, int64_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  int64_t blocks = ceil_div(n, 256);
+  if (blocks > 8192) blocks = 8192;
+  cast_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(src, dst, dt, n);
+  return cudaGetLastError();
+}
+
+__global__ void zero_kernel(void* dst, int dt, int64_t rows, int64_t cols, int64_t ld) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < rows * cols;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    store_d(dst, dt, (i / cols) * ld + i % cols, 0.0);
+}
+
+cudaError_t zero_rows(void* dst, int dt, int64_t rows, int64_t cols, int64_t ld, cudaStream_t st) {
+  if (rows * cols == 0) return cudaSuccess;
+  int64_t blocks = ceil_div(rows * cols, 256);
+  if (blocks > 8192) blocks = 8192;
+  zero_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(dst, dt, rows, cols, ld);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ MSE epilogue
+// raw_n = mean_d (O - t)^2 + z * lse^2  (swvr/api.py:54-56); one warp per row.
+template <typename T>
+__device__ __forceinline__ T row_raw(const T* O, const T* t, const T* lse, int64_t n, int64_t D, T z, int lane) {
+  T s = 0;
+  for (int64_t d = lane; d < D; d += 32) {
+    const T e = O[n * D + d] - t[n * D + d];
+    s += e * e;
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  T raw = s / static_cast<T>(D);
+  if (z != T(0)) raw += z * lse[n] * lse[n];
+  return raw;
+}
+
+template <typename T>
+__global__ void mse_none_kernel(int64_t N, int64_t D, const T* O, const T* lse, const T* t, const T* w, T z, T* out) {
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+  if (n >= N) return;
+  const T raw = row_raw<T>(O, t, lse, n, D, z, threadIdx.x % 32);
+  if (threadIdx.x % 32 == 0) out[n] = w ? raw * w[n] : raw;
+}
+
+// One block, fixed summation order: out[0] = loss; stats[0] = sum(w * raw), stats[1] = denom.
+template <typename T>
+__global__ void __launch_bounds__(1024) mse_reduce_kernel(int64_t N, int64_t D, const T* O, const T* lse, const T* t,
+                                                          const T* w, T z, int reduction, T* out, T* stats) {
+  __shared__ T sh_s[32], sh_w[32];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  T s = 0, ws = 0;
+  for (int64_t n = warp; n < N; n += 32) {
+    const T raw = row_raw<T>(O, t, lse, n, D, z, lane);
+    const T wn = w ? w[n] : T(1);
+    s += raw * wn;
+    ws += wn;
+  }
+  if (lane == 0) {
+    sh_s[warp] = s;
+    sh_w[warp] = ws;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T S = 0, Wt = 0;
+    for (int i = 0; i < 32; ++i) {
+      S += sh_s[i];
+      Wt += sh_w[i];
+    }
+    T denom = T(1);
+    if (reduction == SWVR_REDUCE_MEAN) denom = w ? Wt : static_cast<T>(N);
+    out[0] = S / denom;
+    if (stats) {
+      stats[0] = S;
+      stats[1] = denom;
+    }
+  }
+}
+
+template <typename T>
+__global__ void mse_bwd_kernel(int64_t N, int64_t D, const T* O, const T* lse, const T* t, const T* w, T z,
+                               int reduction, const T* gout, const T* stats, T* gO, T* glse, T* gt, T* gw) {
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (n >= N) return;
+  const T g = reduction == SWVR_REDUCE_NONE ? gout[n] : gout[0];
+  const T wn = w ? w[n] : T(1);
+  T denom = T(1);
+  if (reduction == SWVR_REDUCE_MEAN) denom = stats[1];
+  const T c = g * wn / denom;
+  const T k = c * static_cast<T>(2) / static_cast<T>(D);
+  for (int64_t d = lane; d < D; d += 32) {
+    const T v = k * (O[n * D + d] - t[n * D + d]);
+    gO[n * D + d] = v;
+    if (gt) gt[n * D + d] = -v;
+  }
+  if (lane == 0) glse[n] = c * static_cast<T>(2) * z * lse[n];
+  if (gw) {
+    const T raw = row_raw<T>(O, t, lse, n, D, z, lane);
+    if (lane == 0) {
+      T v = g * raw;
+      if (reduction == SWVR_REDUCE_MEAN) v = g * (raw - stats[0] / denom) / denom;
+      gw[n] = v;
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t mse_fwd_t(int64_t N, int64_t D, const void* O, const void* lse, const void* t, const void* w,
+                             double z, int red, void* out, void* stats, cudaStream_t st) {
+  if (red == SWVR_REDUCE_NONE) {
+    if (N == 0) return cudaSuccess;
+    mse_none_kernel<T><<<static_cast<unsigned>(ceil_div(N, 8)), 256, 0, st>>>(
+        N, D, static_cast<const T*>(O), static_cast<const T*>(lse), static_cast<const T*>(t),
+        static_cast<const T*>(w), static_cast<T>(z), static_cast<T*>(out));
+  } else {
+    mse_reduce_kernel<T><<<1, 1024, 0, st>>>(N, D, static_cast<const T*>(O), static_cast<const T*>(lse),
+                                              static_cast<const T*>(t), static_cast<const T*>(w), static_cast<T>(z),
+                                              red, static_cast<T*>(out), static_cast<T*>(stats));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t mse_fwd(int dt, int64_t N, int64_t D, const void* O, const void* lse, const void* t, const void* w,
+                    double z, int red, void* out, void* stats, cudaStream_t st) {
+  return dt == SWVR_F64 ? mse_fwd_t<double>(N, D, O, lse, t, w, z, red, out, stats, st)
+                        : mse_fwd_t<float>(N, D, O, lse, t, w, z, red, out, stats, st);
+}
+
+template <typename T>
+static cudaError_t mse_bwd_t(int64_t N, int64_t D, const void* O, const void* lse, const void* t, const void* w,
+                             double z, int red, const void* gout, const void* stats, void* gO, void* glse, void* gt,
+                             void* gw, cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  mse_bwd_kernel<T><<<static_cast<unsigned>(ceil_div(N, 8)), 256, 0, st>>>(
+      N, D, static_cast<const T*>(O), static_cast<const T*>(lse), static_cast<const T*>(t), static_cast<const T*>(w),
+      static_cast<T>(z), red, static_cast<const T*>(gout), static_cast<const T*>(stats), static_cast<T*>(gO),
+      static_cast<T*>(glse), static_cast<T*>(gt), static_cast<T*>(gw));
+  return cudaGetLastError();
+}
+
+cudaError_t mse_bwd(int dt, int64_t N, int64_t D, const void* O, const void* lse, const void* t, const void* w,
+                    double z, int red, const void* gout, const void* stats, void* gO, void* glse, void* gt, void* gw,
+                    cudaStream_t st) {
+  return dt == SWVR_F64 ? mse_bwd_t<double>(N, D, O, lse, t, w, z, red, gout, stats, gO, glse, gt, gw, st)
+                        : mse_bwd_t<float>(N, D, O, lse, t, w, z, red, gout, stats, gO, glse, gt, gw, st);
+}
+
+}  // namespace small
+}  // namespace swvr

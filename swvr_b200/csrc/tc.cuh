@@ -1,0 +1,76 @@
+// Host/device declarations shared by the tcgen05 (tensor-core) kernels.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace swvr {
+namespace tc {
+
+// ------------------------------------------------------------------ forward
+struct FwdParams {
+  int N, K, V, D;
+  float sc2;  // logit_scale * log2(e)
+  const void* bias;
+  int bias_dt;
+  int MT, VT;             // 128-token tiles, vocabulary tiles
+  int splits, per, units; // vocabulary splits per token tile, tiles per split, MT * splits
+  float* part_m2;         // [units * 128]
+  float* part_l;          // [units * 128]
+  float* part_acc;        // [units * 128 * D]
+};
+
+struct FwdMaps {
+  CUtensorMap h, w, e;
+};
+
+int fwd_vocab_tile(int DP);
+cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int grid, cudaStream_t st);
+
+// ------------------------------------------------------------------ backward: scores tile kernel
+struct BwdScoresParams {
+  int N, K, D;
+  int v_begin, v_end;  // this chunk's vocabulary rows
+  float scale, sc2;    // logit_scale, logit_scale * log2(e)
+  const void* bias;
+  int bias_dt;
+  const float* lse;    // [N]
+  const float* delta;  // [N]
+  int NT, VT;          // 128-token tiles, 128-row vocabulary tiles of the chunk
+  int TS, per_t, units;  // token splits, token tiles per split, VT * TS
+  void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null
+  int64_t ld_ds;
+  float* part_de;      // [units * 128 * D] or null
+  float* part_db;      // [units * 128] or null
+};
+
+struct BwdScoresMaps {
+  CUtensorMap w, h, e, go;
+};
+
+cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
+                                     int grid, cudaStream_t st);
+
+// ------------------------------------------------------------------ backward: dW / dh GEMMs
+struct GemmParams {
+  int dw_tiles, dh_tiles;    // number of 128x256 output tiles of each problem
+  int dw_mt, dw_nt, dw_kb;   // dW: row tiles (chunk rows / 128), column tiles (K / 256), k-blocks (tokens / 64)
+  int dh_mt, dh_nt, dh_kb;   // dh: row tiles (tokens / 128), column tiles, k-blocks (chunk rows / 64)
+  int v_begin;               // first vocabulary row of the chunk
+  int gw_f32;                // dW output is fp32 (else the 16-bit compute dtype)
+};
+
+struct GemmMaps {
+  CUtensorMap ds_k;   // dS^T as a K-major A operand (dW), box {64, 128}
+  CUtensorMap ds_mn;  // dS^T as an MN-major A operand (dh), box {64, 64}
+  CUtensorMap h_mn;   // h as an MN-major B operand (dW), box {64, 64}
+  CUtensorMap w_mn;   // W as an MN-major B operand (dh), box {64, 64}
+  CUtensorMap gw;     // dW output (TMA store), box {64 or 32, 128}
+  CUtensorMap dh;     // fp32 dh accumulator (TMA reduce-add), box {32, 128}
+};
+
+cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int grid, cudaStream_t st);
+
+}  // namespace tc
+}  // namespace swvr

@@ -1,0 +1,319 @@
+// Tensor-core (tcgen05) backward score kernel on sm_100a, vocabulary-major.
+//
+// A CTA owns a 128-row vocabulary tile of the current chunk (the MMA M dimension, one
+// TMEM lane and one thread per vocabulary row) and walks a range of 128-token tiles:
+//   S^T  = W_tile . h_tile^T                 (K = hidden; recompute of the forward scores)
+//   dP^T = E_tile . dO_tile^T                (K = D)
+//   P    = 2^(S*s*log2e + b*log2e - LSE*log2e),   dS = P * (dP - delta)
+//   db  += rowsum(dS)                        (thread-local: the thread owns the row)
+//   dE  += P^T . dO_tile                     (tcgen05.mma, A = P read from TMEM, D in TMEM)
+//   dS^T * s is stored in the compute dtype for the dh / dW GEMMs (tc_gemm.cu).
+// dE and db of a unit go to a partial slot; reduce_de_db_kernel (small.cu) sums the token
+// splits of a vocabulary row in a fixed order, so the result is deterministic.
+//
+// Replaces the reference's per-chunk recompute GEMM + Triton _bwd_chunk_kernel
+// (swvr/chunked.py:120-131, swvr/triton_kernels.py:76-118).
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace swvr {
+namespace tc {
+
+template <bool kBF16, int DP, int NS>
+struct BwdCfg {
+  static constexpr int BOX = 128 * 128;  // 128 rows x 128 bytes (64 16-bit elements)
+  static constexpr int A_BYTES = BOX, B_BYTES = BOX;
+  static constexpr int E_BYTES = (DP / 64) * BOX;
+  static constexpr int GO_BYTES = (DP / 64) * BOX;
+  static constexpr int SMEM_A = 0;
+  static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
+  static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
+  static constexpr int SMEM_GO = SMEM_E + E_BYTES;
+  static constexpr int SMEM_LSE = SMEM_GO + 2 * GO_BYTES;
+  static constexpr int SMEM_DELTA = SMEM_LSE + 512;
+  static constexpr int SMEM_BAR = SMEM_DELTA + 512;
+  static constexpr int NBAR = 2 * NS + 13;
+  static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
+  static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
+  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;
+  static_assert(DE_COL + DP <= 512, "TMEM budget");
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+template <bool kBF16, int DP, int NS>
+__global__ void __launch_bounds__(256, 1)
+    bwd_scores_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_h,
+                      const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_go,
+                      const BwdScoresParams p) {
+  using Cfg = BwdCfg<kBF16, DP, NS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NS;
+  uint64_t* e_full = bars + 2 * NS;
+  uint64_t* e_empty = e_full + 1;
+  uint64_t* go_full = e_empty + 1;    // [2]
+  uint64_t* go_empty = go_full + 2;   // [2]
+  uint64_t* s_full = go_empty + 2;    // [2]
+  uint64_t* dp_full = s_full + 2;
+  uint64_t* p_ready = dp_full + 1;    // [2]
+  uint64_t* de_full = p_ready + 2;
+  uint64_t* de_free = de_full + 1;
+  uint64_t* spare = de_free + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* lse_s = reinterpret_cast<float*>(smem + Cfg::SMEM_LSE);
+  float* delta_s = reinterpret_cast<float*>(smem + Cfg::SMEM_DELTA);
+
+  const bool need_ds = p.ds != nullptr, need_de = p.part_de != nullptr, need_db = p.part_db != nullptr;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(e_full, 1);
+    mbar_init(e_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&go_full[b], 1);
+      mbar_init(&go_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_ready[b], 128);
+    }
+    mbar_init(dp_full, 1);
+    mbar_init(de_full, 1);
+    mbar_init(de_free, 128);
+    mbar_init(spare, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_h);
+    tma_prefetch_desc(&tm_e);
+    tma_prefetch_desc(&tm_go);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int KB = (p.K + 63) / 64;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int vt = u / p.TS, ts = u % p.TS;
+        const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+        if (it1 <= it0) continue;
+        const int vrow0 = p.v_begin + vt * 128;
+        if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
+        mbar_arrive_expect_tx(e_full, Cfg::E_BYTES);
+#pragma unroll
+        for (int c = 0; c < DP / 64; ++c) tma_load_2d(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, e_full, c * 64, vrow0);
+        for (int it = it0; it < it1; ++it, ++g) {
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrBwdScores | 2)) goto done;
+            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+            tma_load_2d(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES, &tm_w, &full[stage], kb * 64, vrow0);
+            tma_load_2d(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES, &tm_h, &full[stage], kb * 64, it * 128);
+            if (++stage == NS) {
+              stage = 0;
+              sphase ^= 1u;
+            }
+          }
+          const uint32_t gb = g & 1u, use = g >> 1;
+          if (!mbar_wait(&go_empty[gb], (use & 1u) ^ 1u, abort_flag, kErrBwdScores | 3)) goto done;
+          mbar_arrive_expect_tx(&go_full[gb], Cfg::GO_BYTES);
+#pragma unroll
+          for (int c = 0; c < DP / 64; ++c)
+            tma_load_2d(smem + Cfg::SMEM_GO + gb * Cfg::GO_BYTES + c * Cfg::BOX, &tm_go, &go_full[gb], c * 64,
+                        it * 128);
+        }
+        ++uc;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idS = idesc_f16(kBF16, 128, 128, false, false);
+      const uint32_t idDE = idesc_f16(kBF16, 128, DP, false, true);
+      uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
+      const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E);
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int ts = u % p.TS;
+        const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+        const int n = it1 - it0;
+        if (n <= 0) continue;
+        if (!mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 4)) goto done;
+        tc_fence_after();
+        for (int j = 0; j <= n; ++j) {
+          if (j < n) {
+            const uint32_t b = g & 1u;
+            for (int kb = 0; kb < KB; ++kb) {
+              if (!mbar_wait(&full[stage], sphase, abort_flag, kErrBwdScores | 5)) goto done;
+              tc_fence_after();
+              const uint32_t abase = smem_u32(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES);
+              const uint32_t bbase = smem_u32(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                umma_ss(tmem + Cfg::S_COL + b * 128, sdesc_sw128(abase + ks * 32, 16, 1024),
+                        sdesc_sw128(bbase + ks * 32, 16, 1024), idS, (kb | ks) ? 1u : 0u);
+              umma_commit(&empty[stage]);
+              if (++stage == NS) {
+                stage = 0;
+                sphase ^= 1u;
+              }
+            }
+            umma_commit(&s_full[b]);
+            // dP^T = E . dO^T into the single dP buffer: the previous tile's gradient pass
+            // must have finished reading it.
+            if (j > 0 && !mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 6))
+              goto done;
+            if (!mbar_wait(&go_full[b], (g >> 1) & 1u, abort_flag, kErrBwdScores | 7)) goto done;
+            tc_fence_after();
+            const uint32_t gobase = smem_u32(smem + Cfg::SMEM_GO + b * Cfg::GO_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < DP / 16; ++ks)
+              umma_ss(tmem + Cfg::DP_COL, sdesc_sw128(ebase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024),
+                      sdesc_sw128(gobase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024), idS, ks ? 1u : 0u);
+            umma_commit(dp_full);
+            ++g;
+          }
+          if (j > 0) {
+            const uint32_t gg = g - 1u - (j < n ? 1u : 0u);
+            const uint32_t bb = gg & 1u;
+            if (j == n && !mbar_wait(&p_ready[bb], (gg >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+            if (need_de) {
+              const bool first = (j == 1);
+              if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
+              tc_fence_after();
+              const uint32_t gobase = smem_u32(smem + Cfg::SMEM_GO + bb * Cfg::GO_BYTES);
+#pragma unroll
+              for (int ks = 0; ks < 8; ++ks)
+                umma_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + bb * 128 + ks * 8,
+                        sdesc_sw128(gobase + ks * 2048, Cfg::BOX, 1024), idDE, (first && ks == 0) ? 0u : 1u);
+            }
+            umma_commit(&go_empty[bb]);
+          }
+        }
+        umma_commit(e_empty);
+        if (need_de) umma_commit(de_full);
+        ++uc;
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- gradient warps
+    const int r = threadIdx.x - 128;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    uint32_t g = 0, uc = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      const int vt = u / p.TS, ts = u % p.TS;
+      const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+      if (it1 <= it0) continue;
+      const int vrow = p.v_begin + vt * 128 + r;
+      const bool vvalid = vrow < p.v_end;
+      const float b2 = (p.bias != nullptr && vvalid) ? load_f(p.bias, p.bias_dt, vrow) * kLog2e : 0.f;
+      float db = 0.f;
+      for (int it = it0; it < it1; ++it, ++g) {
+        const int t0 = it * 128;
+        named_bar_sync(1, 128);
+        {
+          const int t = t0 + r;
+          lse_s[r] = t < p.N ? p.lse[t] * kLog2e : INFINITY;
+          delta_s[r] = t < p.N ? p.delta[t] : 0.f;
+        }
+        named_bar_sync(1, 128);
+        const uint32_t b = g & 1u;
+        if (!warp_wait(&s_full[b], (g >> 1) & 1u, abort_flag, kErrBwdScores | 10)) goto done;
+        if (!warp_wait(dp_full, g & 1u, abort_flag, kErrBwdScores | 11)) goto done;
+        tc_fence_after();
+        const uint32_t sbase = trow + Cfg::S_COL + b * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t s[32], dp[32];
+          tmem_ld32(sbase + c * 32, s);
+          tmem_ld32(trow + Cfg::DP_COL + c * 32, dp);
+          tmem_wait_ld();
+          uint32_t pk_p[16], pk_ds[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int tt = c * 32 + i;
+            const float p0 = ex2(fmaf(__uint_as_float(s[i]), p.sc2, b2) - lse_s[tt]);
+            const float p1 = ex2(fmaf(__uint_as_float(s[i + 1]), p.sc2, b2) - lse_s[tt + 1]);
+            const float d0 = p0 * (__uint_as_float(dp[i]) - delta_s[tt]);
+            const float d1 = p1 * (__uint_as_float(dp[i + 1]) - delta_s[tt + 1]);
+            db += d0 + d1;
+            pk_ds[i / 2] = pack2<kBF16>(d0 * p.scale, d1 * p.scale);
+            pk_p[i / 2] = pack2<kBF16>(p0, p1);
+          }
+          if (need_ds && vvalid) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.ds) +
+                                                  static_cast<int64_t>(vrow - p.v_begin) * p.ld_ds + t0 + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
+          }
+          if (need_de) tmem_st16(sbase + c * 16, pk_p);
+        }
+        if (need_de) tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[b]);
+      }
+      const int64_t slot = static_cast<int64_t>(u) * 128 + r;
+      if (need_de) {
+        if (!warp_wait(de_full, uc & 1u, abort_flag, kErrBwdScores | 12)) goto done;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(trow + Cfg::DE_COL + c * 32, o);
+          tmem_wait_ld();
+          if (vvalid) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int d = c * 32 + i;
+              if (d < p.D) p.part_de[slot * p.D + d] = __uint_as_float(o[i]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(de_free);
+      }
+      if (need_db && vvalid) p.part_db[slot] = db;
+      ++uc;
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_after_abort(warp == 1 && lane == 0, spare);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool kBF16, int DP, int NS>
+static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int grid, cudaStream_t st) {
+  using Cfg = BwdCfg<kBF16, DP, NS>;
+  auto kern = bwd_scores_kernel<kBF16, DP, NS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(m.w, m.h, m.e, m.go, prm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
+                                     int grid, cudaStream_t st) {
+  if (DP == 64) return bf16 ? launch_bwd<true, 64, 4>(maps, prm, grid, st) : launch_bwd<false, 64, 4>(maps, prm, grid, st);
+  return bf16 ? launch_bwd<true, 128, 4>(maps, prm, grid, st) : launch_bwd<false, 128, 4>(maps, prm, grid, st);
+}
+
+}  // namespace tc
+}  // namespace swvr

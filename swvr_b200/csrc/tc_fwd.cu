@@ -1,0 +1,324 @@
+// Tensor-core (tcgen05) forward of the softmax readout on sm_100a.
+//
+// One CTA per SM walks work units (a 128-token tile x a contiguous range of vocabulary
+// tiles).  Per vocabulary tile j:
+//   S_j  = h_tile . W_j^T            tcgen05.mma, A/B from 128B-swizzled smem, D in TMEM
+//   P_j  = 2^(S_j*s*log2e + b*log2e - m_ref), rounded to bf16/fp16 and stored back into
+//          TMEM over S_j
+//   O   += P_j . E_j                 tcgen05.mma with A read from TMEM
+// so neither S nor P ever leaves the SM.  Warp roles: warp 0 issues TMA loads, warp 1
+// (one thread) issues MMAs, warps 4-7 run the online softmax with one thread per token
+// row (TMEM lane = row, so row max / row sum are thread-local).  S is double-buffered in
+// TMEM, so the MMAs of tile j+1 overlap the softmax of tile j.  The running reference max
+// m_ref is only raised when a tile's max exceeds it by more than 2^8 (the result is
+// exact either way because l and O share m_ref); then O is rescaled in TMEM.
+//
+// Each unit writes its per-row state (m_ref in log2 units, l, O-accumulator) to a partial
+// slot; combine_kernel (small.cu) merges the slots of a row in a fixed order.
+//
+// This replaces the reference's per-chunk cuBLAS S GEMM + Triton _fwd_chunk_kernel
+// (swvr/chunked.py:89-95, swvr/triton_kernels.py:37-73) with one fused kernel.
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace swvr {
+namespace tc {
+
+template <bool kBF16, int BV, int DP, int NS>
+struct FwdCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BV * BK * 2;
+  static constexpr int E_BOX = BV * 128;  // one 64-column box of the E tile
+  static constexpr int E_BYTES = (DP / 64) * E_BOX;
+  static constexpr int SMEM_A = 0;
+  static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
+  static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
+  static constexpr int SMEM_BAR = SMEM_E + 2 * E_BYTES;
+  static constexpr int NBAR = 2 * NS + 11;  // last one: abort drain
+  static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
+  static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
+  static constexpr uint32_t O_COL = 2 * BV;
+  static_assert(2 * BV + DP <= 512, "TMEM budget");
+  static_assert(BV % 32 == 0 && BV <= 256, "vocab tile");
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0 && E_BOX % 1024 == 0, "1024-byte alignment");
+};
+
+__device__ __forceinline__ float bias2_at(const FwdParams& p, int col) {
+  if (p.bias == nullptr || col >= p.V) return 0.f;
+  return load_f(p.bias, p.bias_dt, col) * kLog2e;
+}
+
+template <bool kBF16, int BV, int DP, int NS>
+__global__ void __launch_bounds__(256, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_w,
+               const __grid_constant__ CUtensorMap tm_e, const FwdParams p) {
+  using Cfg = FwdCfg<kBF16, BV, DP, NS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NS;
+  uint64_t* s_full = bars + 2 * NS;
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* e_full = p_ready + 2;
+  uint64_t* e_empty = e_full + 2;
+  uint64_t* pe_done = e_empty + 2;
+  uint64_t* o_free = pe_done + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_ready[b], 128);
+      mbar_init(&e_full[b], 1);
+      mbar_init(&e_empty[b], 1);
+    }
+    mbar_init(pe_done, 1);
+    mbar_init(o_free, 128);
+    mbar_init(&bars[Cfg::NBAR - 1], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_h);
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_e);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int KB = (p.K + 63) / 64;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      uint32_t stage = 0, sphase = 0, g = 0;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int mt = u / p.splits, sp = u % p.splits;
+        const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
+        for (int vt = vt0; vt < vt1; ++vt, ++g) {
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrFwd | 1)) goto done;
+            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+            tma_load_2d(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES, &tm_h, &full[stage], kb * 64, mt * 128);
+            tma_load_2d(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES, &tm_w, &full[stage], kb * 64, vt * BV);
+            if (++stage == NS) {
+              stage = 0;
+              sphase ^= 1u;
+            }
+          }
+          const uint32_t eb = g & 1u, use = g >> 1;
+          if (!mbar_wait(&e_empty[eb], (use & 1u) ^ 1u, abort_flag, kErrFwd | 2)) goto done;
+          mbar_arrive_expect_tx(&e_full[eb], Cfg::E_BYTES);
+#pragma unroll
+          for (int c = 0; c < DP / 64; ++c)
+            tma_load_2d(smem + Cfg::SMEM_E + eb * Cfg::E_BYTES + c * Cfg::E_BOX, &tm_e, &e_full[eb], c * 64, vt * BV);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idS = idesc_f16(kBF16, 128, BV, false, false);
+      const uint32_t idPE = idesc_f16(kBF16, 128, DP, false, true);
+      uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        const int sp = u % p.splits;
+        const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
+        const int ntiles = vt1 - vt0;
+        if (ntiles <= 0) continue;
+        for (int j = 0; j <= ntiles; ++j) {
+          if (j < ntiles) {
+            const uint32_t b = g & 1u;
+            for (int kb = 0; kb < KB; ++kb) {
+              if (!mbar_wait(&full[stage], sphase, abort_flag, kErrFwd | 3)) goto done;
+              tc_fence_after();
+              const uint32_t abase = smem_u32(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES);
+              const uint32_t bbase = smem_u32(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                umma_ss(tmem + b * BV, sdesc_sw128(abase + ks * 32, 16, 1024), sdesc_sw128(bbase + ks * 32, 16, 1024),
+                        idS, (kb | ks) ? 1u : 0u);
+              umma_commit(&empty[stage]);
+              if (++stage == NS) {
+                stage = 0;
+                sphase ^= 1u;
+              }
+            }
+            umma_commit(&s_full[b]);
+            ++g;
+          }
+          if (j > 0) {
+            // O += P . E for the previous tile (its softmax overlapped the MMAs just issued)
+            const uint32_t gg = g - 1u - (j < ntiles ? 1u : 0u);
+            const uint32_t bb = gg & 1u, use = gg >> 1;
+            const bool first = (j == 1);
+            if (!mbar_wait(&p_ready[bb], use & 1u, abort_flag, kErrFwd | 4)) goto done;
+            if (!mbar_wait(&e_full[bb], use & 1u, abort_flag, kErrFwd | 5)) goto done;
+            if (first && uc > 0 && !mbar_wait(o_free, (uc - 1u) & 1u, abort_flag, kErrFwd | 6)) goto done;
+            tc_fence_after();
+            const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E + bb * Cfg::E_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < BV / 16; ++ks)
+              umma_ts(tmem + Cfg::O_COL, tmem + bb * BV + ks * 8, sdesc_sw128(ebase + ks * 2048, Cfg::E_BOX, 1024),
+                      idPE, (first && ks == 0) ? 0u : 1u);
+            umma_commit(pe_done);
+            umma_commit(&e_empty[bb]);
+          }
+        }
+        ++uc;
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- softmax warps
+    const int r = threadIdx.x - 128;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t trow = tmem + lane_base;
+    uint32_t g = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      const int mt = u / p.splits, sp = u % p.splits;
+      const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
+      if (vt1 <= vt0) continue;
+      const int n = mt * 128 + r;
+      float m2 = -INFINITY, l = 0.f;
+      for (int vt = vt0; vt < vt1; ++vt, ++g) {
+        const uint32_t b = g & 1u;
+        const bool not_first = vt > vt0;
+        if (!warp_wait(&s_full[b], (g >> 1) & 1u, abort_flag, kErrFwd | 7)) goto done;
+        tc_fence_after();
+        const uint32_t sbase = trow + b * BV;
+        const int v0 = vt * BV;
+        // pass 1: row max of this tile (log2 units)
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < BV / 32; ++c) {
+          uint32_t x[32];
+          tmem_ld32(sbase + c * 32, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = v0 + c * 32 + i;
+            const float t = col < p.V ? fmaf(__uint_as_float(x[i]), p.sc2, bias2_at(p, col)) : -INFINITY;
+            mx = fmaxf(mx, t);
+          }
+        }
+        // the previous tile's P.E must be done before O is touched (consumes one completion)
+        if (not_first) {
+          if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 8)) goto done;
+          tc_fence_after();
+        }
+        const bool resc = mx > m2 + 8.f;
+        float alpha = 1.f;
+        if (resc) {
+          alpha = ex2(m2 - mx);
+          m2 = mx;
+          l *= alpha;
+        }
+        if (not_first && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int c = 0; c < DP / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(trow + Cfg::O_COL + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(trow + Cfg::O_COL + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        const float ref = (m2 == -INFINITY) ? 0.f : m2;
+        // pass 2: P = 2^(t - ref), row sum, P (16-bit) back into TMEM over S
+#pragma unroll 1
+        for (int c = 0; c < BV / 32; ++c) {
+          uint32_t x[32];
+          tmem_ld32(sbase + c * 32, x);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = v0 + c * 32 + i;
+            const float t0 = col < p.V ? fmaf(__uint_as_float(x[i]), p.sc2, bias2_at(p, col)) : -INFINITY;
+            const float t1 = col + 1 < p.V ? fmaf(__uint_as_float(x[i + 1]), p.sc2, bias2_at(p, col + 1)) : -INFINITY;
+            const float p0 = ex2(t0 - ref), p1 = ex2(t1 - ref);
+            l += p0 + p1;
+            pk[i / 2] = pack2<kBF16>(p0, p1);
+          }
+          tmem_st16(sbase + c * 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[b]);
+      }
+      // unit end: wait for the last P.E, then write this unit's partial state
+      if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 9)) goto done;
+      tc_fence_after();
+      {
+        const int64_t slot = static_cast<int64_t>(u) * 128 + r;
+#pragma unroll 1
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(trow + Cfg::O_COL + c * 32, o);
+          tmem_wait_ld();
+          if (n < p.N) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int d = c * 32 + i;
+              if (d < p.D) p.part_acc[slot * p.D + d] = __uint_as_float(o[i]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(o_free);
+        if (n < p.N) {
+          p.part_m2[slot] = m2;
+          p.part_l[slot] = l;
+        }
+      }
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_after_abort(warp == 1 && lane == 0, &bars[Cfg::NBAR - 1]);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------- host
+template <bool kBF16, int BV, int DP, int NS>
+static cudaError_t launch_fwd(const FwdMaps& maps, const FwdParams& prm, int grid, cudaStream_t st) {
+  using Cfg = FwdCfg<kBF16, BV, DP, NS>;
+  auto kern = fwd_kernel<kBF16, BV, DP, NS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(maps.h, maps.w, maps.e, prm);
+  return cudaGetLastError();
+}
+
+int fwd_vocab_tile(int DP) { return DP <= 64 ? 192 : 160; }
+
+cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int grid,
+                              cudaStream_t st) {
+  if (DP == 64) {
+    return bf16 ? launch_fwd<true, 192, 64, 4>(maps, prm, grid, st) : launch_fwd<false, 192, 64, 4>(maps, prm, grid, st);
+  }
+  return bf16 ? launch_fwd<true, 160, 128, 4>(maps, prm, grid, st) : launch_fwd<false, 160, 128, 4>(maps, prm, grid, st);
+}
+
+}  // namespace tc
+}  // namespace swvr

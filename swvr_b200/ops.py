@@ -1,0 +1,337 @@
+"""The readout as opaque ``torch.library`` custom ops backed by the CUDA library.
+
+Same contract as the reference's ``swvr::chunked_fwd`` / ``swvr::chunked_bwd``
+(swvr/chunked.py:157-212): the ops are opaque to ``torch.compile`` (fake impls give shapes),
+the forward saves ``h, W, E, bias, O, LSE``, the backward maps missing upstream grads to
+zeros, frozen inputs skip their work, empty tensors stand for "no gradient", and grads
+come back in each parameter's dtype.  The reference's ``use_triton`` argument is gone:
+there is one implementation, CUDA only, and CPU tensors raise.
+
+Operand preparation is plumbing only: inputs are cast to the compute dtype ``cdt`` (as the
+reference's ``.to(cdt)``) and, on the tensor-core path, re-laid out when a row pitch or base
+address is not 16-byte aligned.  All arithmetic happens in libswvr_b200.so.
+"""
+from __future__ import annotations
+
+import os
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _native as nat
+
+DEFAULT_CHUNK = 8192
+
+
+def acc_dtype(cdt: torch.dtype) -> torch.dtype:
+    """swvr/chunked.py:26-27."""
+    return torch.float64 if cdt == torch.float64 else torch.float32
+
+
+def default_chunk_size() -> int:
+    """swvr/chunked.py:57-59: env ``SWVR_CHUNK`` or 8192."""
+    raw = os.environ.get("SWVR_CHUNK")
+    return int(raw) if raw else DEFAULT_CHUNK
+
+
+def _tensor_core(cdt: torch.dtype) -> bool:
+    return cdt in (torch.bfloat16, torch.float16)
+
+
+def _require_cuda(*tensors) -> torch.device:
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise RuntimeError(
+            "swvr_b200 runs on CUDA devices only (sm_100a); got a tensor on "
+            f"{dev}. There is no CPU fallback.")
+    for t in tensors[1:]:
+        if t is not None and t.device != dev:
+            raise ValueError(f"all inputs must be on {dev}, got one on {t.device}")
+    return dev
+
+
+def _aligned(t: torch.Tensor) -> bool:
+    es = t.element_size()
+    return t.data_ptr() % 16 == 0 and (t.dim() < 2 or (t.stride(0) * es) % 16 == 0 or t.shape[0] <= 1)
+
+
+def _operand(x: torch.Tensor, cdt: torch.dtype, pad_cols: int = 0) -> torch.Tensor:
+    """``x`` in ``cdt`` with a unit last stride (swvr/chunked.py:66-69); for the tensor-core
+    path also a 16-byte aligned base and row pitch, padding the row pitch with zeros."""
+    if x.dtype != cdt:
+        x = x.to(cdt)
+    if x.dim() == 2 and x.shape[1] > 0 and x.stride(1) != 1:
+        x = x.contiguous()
+    if not _tensor_core(cdt):
+        return x
+    rows, cols = x.shape
+    pitch = x.stride(0) if x.stride(0) >= cols else cols
+    need = max(cols + pad_cols, 8)
+    need = (need + 7) // 8 * 8
+    if _aligned(x) and pitch % 8 == 0 and pitch >= need:
+        return x
+    buf = torch.zeros(rows, need, dtype=cdt, device=x.device)
+    buf[:, :cols] = x
+    return buf[:, :cols]
+
+
+def _ld(x: torch.Tensor) -> int:
+    """Row pitch in elements of a 2-D tensor with a unit last stride."""
+    return x.stride(0) if x.stride(0) >= x.shape[1] else max(x.shape[1], 1)
+
+
+def _problem(h, W, E, bias, scale, chunk, cdt) -> nat.Problem:
+    p = nat.Problem()
+    p.n_tokens, p.hidden = h.shape[0], h.shape[1]
+    p.vocab, p.embed_dim = W.shape[0], E.shape[1]
+    p.compute_dtype = nat.dtype_code(cdt)
+    p.bias_dtype = nat.dtype_code(bias.dtype) if bias is not None else 0
+    p.h, p.ldh = h.data_ptr(), _ld(h)
+    p.W, p.ldw = W.data_ptr(), _ld(W)
+    p.E, p.lde = E.data_ptr(), _ld(E)
+    p.bias = bias.data_ptr() if bias is not None else None
+    p.logit_scale = float(scale)
+    p.chunk = int(chunk)
+    return p
+
+
+def _prepare(h, W, E, bias, cdt):
+    """Operands as the library takes them.  K is zero-padded to a multiple of 8 on the
+    tensor-core path (zero columns add nothing to h . W^T)."""
+    K = h.shape[1]
+    if _tensor_core(cdt) and K % 8 != 0:
+        K8 = (K + 7) // 8 * 8
+        h = torch.nn.functional.pad(h.to(cdt), (0, K8 - K))
+        W = torch.nn.functional.pad(W.to(cdt), (0, K8 - K))
+    hc = _operand(h, cdt)
+    Wc = _operand(W, cdt)
+    Ec = _operand(E, cdt)
+    b = bias.contiguous() if bias is not None else None
+    return hc, Wc, Ec, b
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _forward(h, W, E, bias, logit_scale, chunk, cdt):
+    dev = _require_cuda(h, W, E, bias)
+    adt = acc_dtype(cdt)
+    N, V, D = h.shape[0], W.shape[0], E.shape[1]
+    O = torch.empty(N, D, dtype=adt, device=dev)
+    lse = torch.empty(N, dtype=adt, device=dev)
+    if N == 0:
+        return O, lse
+    if V == 0:  # the reference's loop never runs: O = 0 / 0, LSE = -inf + log(0)
+        return O.fill_(float("nan")), lse.fill_(float("-inf"))
+    hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
+    p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
+    lib = nat.lib()
+    nbytes = nat.c_size_t(0)
+    with torch.cuda.device(dev):
+        nat.check(lib.swvr_fwd_workspace_size(p, nat.ctypes.byref(nbytes)), "swvr_fwd_workspace_size")
+        ws = _workspace(nbytes.value, dev)
+        nat.check(lib.swvr_fwd(p, O.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
+                  "swvr_fwd")
+    return O, lse
+
+
+def _grad_buffer(x: torch.Tensor, cdt: torch.dtype, tc: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(buffer the library writes, tensor returned to autograd) for a parameter's gradient."""
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if tc and x.dim() == 2 and x.dtype not in (cdt, torch.float32):
+        buf = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+        return buf, out
+    return out, out
+
+
+def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b):
+    dev = _require_cuda(h, W, E, bias, gO, glse, O, lse)
+    adt = O.dtype
+    tc = _tensor_core(cdt)
+    N, K, V, D = h.shape[0], h.shape[1], W.shape[0], E.shape[1]
+    need_b = need_b and bias is not None
+    gh = torch.empty(h.shape, dtype=h.dtype, device=dev) if need_h else None
+    gW_buf, gW = _grad_buffer(W, cdt, tc) if need_W else (None, None)
+    gE = torch.empty(E.shape, dtype=E.dtype, device=dev) if need_E else None
+    gb = torch.empty(bias.shape, dtype=bias.dtype, device=dev) if need_b else None
+    if not (need_h or need_W or need_E or need_b):
+        return gh, gW, gE, gb
+    if V == 0:
+        if gh is not None:
+            gh.zero_()
+        return gh, gW, gE, gb
+    hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
+    K8 = hc.shape[1]
+    padded_k = K8 != K
+    gh_buf = gh
+    if need_h and padded_k:
+        gh_buf = torch.empty(N, K8, dtype=h.dtype, device=dev)
+    if need_W and padded_k:
+        gW_buf = torch.empty(V, K8, dtype=gW_buf.dtype, device=dev)
+    p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
+    g = nat.Grads()
+    gO = gO.to(adt).contiguous()
+    glse = glse.to(adt).contiguous()
+    g.grad_O, g.grad_lse, g.O, g.lse = gO.data_ptr(), glse.data_ptr(), O.data_ptr(), lse.data_ptr()
+    if gh_buf is not None:
+        g.grad_h, g.grad_h_dtype = gh_buf.data_ptr(), nat.dtype_code(gh_buf.dtype)
+    if gW_buf is not None:
+        g.grad_W, g.grad_W_dtype, g.ld_grad_W = gW_buf.data_ptr(), nat.dtype_code(gW_buf.dtype), gW_buf.shape[1]
+    if gE is not None:
+        g.grad_E, g.grad_E_dtype, g.ld_grad_E = gE.data_ptr(), nat.dtype_code(gE.dtype), max(D, 1)
+    if gb is not None:
+        g.grad_bias, g.grad_bias_dtype = gb.data_ptr(), nat.dtype_code(gb.dtype)
+    lib = nat.lib()
+    nbytes = nat.c_size_t(0)
+    with torch.cuda.device(dev):
+        nat.check(lib.swvr_bwd_workspace_size(p, g, nat.ctypes.byref(nbytes)), "swvr_bwd_workspace_size")
+        ws = _workspace(nbytes.value, dev)
+        nat.check(lib.swvr_bwd(p, g, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)), "swvr_bwd")
+    if need_h and gh_buf is not gh:
+        gh.copy_(gh_buf[:, :K])
+    if need_W and gW_buf is not gW:
+        gW.copy_(gW_buf[:, :K])
+    return gh, gW, gE, gb
+
+
+# The forward and backward are opaque custom ops, so torch.compile cannot see into (and so
+# cannot reorder or materialise) the vocabulary loop; fake impls provide the shapes.
+
+@torch.library.custom_op("swvr_b200::fwd", mutates_args=())
+def _fwd_op(h: torch.Tensor, W: torch.Tensor, E: torch.Tensor, bias: Optional[torch.Tensor],
+            logit_scale: float, chunk: int, cdt: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _forward(h, W, E, bias, logit_scale, chunk, cdt)
+
+
+@_fwd_op.register_fake
+def _(h, W, E, bias, logit_scale, chunk, cdt):
+    adt = acc_dtype(cdt)
+    return h.new_empty(h.shape[0], E.shape[1], dtype=adt), h.new_empty(h.shape[0], dtype=adt)
+
+
+@torch.library.custom_op("swvr_b200::bwd", mutates_args=())
+def _bwd_op(gO: torch.Tensor, glse: torch.Tensor, h: torch.Tensor, W: torch.Tensor, E: torch.Tensor,
+            bias: Optional[torch.Tensor], O: torch.Tensor, lse: torch.Tensor, logit_scale: float, chunk: int,
+            cdt: torch.dtype, need_h: bool, need_W: bool, need_E: bool, need_b: bool) -> List[torch.Tensor]:
+    grads = _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b)
+    # custom ops cannot return None; an empty tensor stands for "no gradient"
+    return [gr if gr is not None else h.new_empty(0) for gr in grads]
+
+
+@_bwd_op.register_fake
+def _(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b):
+    like = [(need_h, h), (need_W, W), (need_E, E), (need_b and bias is not None, bias)]
+    return [torch.empty_like(x) if need else h.new_empty(0) for need, x in like]
+
+
+def _setup_context(ctx, inputs, output):
+    h, W, E, bias, logit_scale, chunk, cdt = inputs
+    O, lse = output
+    ctx.save_for_backward(h, W, E, bias, O, lse)
+    ctx.args = (logit_scale, chunk, cdt)
+
+
+def _autograd_backward(ctx, gO, glse):
+    h, W, E, bias, O, lse = ctx.saved_tensors
+    needs = [bool(n) for n in ctx.needs_input_grad[:4]]
+    needs[3] = needs[3] and bias is not None
+    gO = gO if gO is not None else torch.zeros_like(O)
+    glse = glse if glse is not None else torch.zeros_like(lse)
+    grads = _bwd_op(gO, glse, h, W, E, bias, O, lse, *ctx.args, *needs)
+    return (*[gr if need else None for gr, need in zip(grads, needs)], None, None, None)
+
+
+_fwd_op.register_autograd(_autograd_backward, setup_context=_setup_context)
+
+
+def softmax_readout_op(h2, W, E, bias, logit_scale, chunk, cdt):
+    """``h2`` is ``[N, K]``; returns ``(O [N, D], LSE [N])`` in the accumulation dtype.
+
+    Autocast is disabled inside, as in swvr/chunked.py:208-212.
+    """
+    with torch.autocast(h2.device.type, enabled=False):
+        return _fwd_op(h2, W, E, bias, float(logit_scale), int(chunk), cdt)
+
+
+# ------------------------------------------------------------------ MSE / z-loss / weight epilogue
+
+_REDUCTIONS = {"none": nat.REDUCE_NONE, "sum": nat.REDUCE_SUM, "mean": nat.REDUCE_MEAN}
+
+
+@torch.library.custom_op("swvr_b200::mse", mutates_args=())
+def _mse_op(O: torch.Tensor, lse: torch.Tensor, target: torch.Tensor, weight: Optional[torch.Tensor],
+            z_loss_weight: float, reduction: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(O, lse, target, weight)
+    N, D = O.shape
+    out = torch.empty((N,) if reduction == nat.REDUCE_NONE else (), dtype=O.dtype, device=dev)
+    stats = torch.zeros(2, dtype=O.dtype, device=dev)
+    with torch.cuda.device(dev):
+        nat.check(nat.lib().swvr_mse_fwd(N, D, nat.dtype_code(O.dtype), O.data_ptr(), lse.data_ptr(),
+                                         target.data_ptr(), nat.ptr(weight), float(z_loss_weight), int(reduction),
+                                         out.data_ptr(), stats.data_ptr(), nat.stream_ptr(dev)), "swvr_mse_fwd")
+    return out, stats
+
+
+@_mse_op.register_fake
+def _(O, lse, target, weight, z_loss_weight, reduction):
+    shape = (O.shape[0],) if reduction == nat.REDUCE_NONE else ()
+    return O.new_empty(shape), O.new_empty(2)
+
+
+@torch.library.custom_op("swvr_b200::mse_bwd", mutates_args=())
+def _mse_bwd_op(grad: torch.Tensor, O: torch.Tensor, lse: torch.Tensor, target: torch.Tensor,
+                weight: Optional[torch.Tensor], stats: torch.Tensor, z_loss_weight: float, reduction: int,
+                need_target: bool, need_weight: bool) -> List[torch.Tensor]:
+    dev = _require_cuda(O, lse, target, weight, grad)
+    N, D = O.shape
+    grad = grad.to(O.dtype).contiguous()
+    gO = torch.empty_like(O)
+    glse = torch.empty_like(lse)
+    gt = torch.empty_like(O) if need_target else None
+    gw = torch.empty(N, dtype=O.dtype, device=dev) if (need_weight and weight is not None) else None
+    with torch.cuda.device(dev):
+        nat.check(nat.lib().swvr_mse_bwd(N, D, nat.dtype_code(O.dtype), O.data_ptr(), lse.data_ptr(),
+                                         target.data_ptr(), nat.ptr(weight), float(z_loss_weight), int(reduction),
+                                         grad.data_ptr(), stats.data_ptr(), gO.data_ptr(), glse.data_ptr(),
+                                         nat.ptr(gt), nat.ptr(gw), nat.stream_ptr(dev)), "swvr_mse_bwd")
+    return [gO, glse, gt if gt is not None else O.new_empty(0), gw if gw is not None else O.new_empty(0)]
+
+
+@_mse_bwd_op.register_fake
+def _(grad, O, lse, target, weight, stats, z_loss_weight, reduction, need_target, need_weight):
+    return [torch.empty_like(O), torch.empty_like(lse),
+            torch.empty_like(O) if need_target else O.new_empty(0),
+            O.new_empty(O.shape[0]) if (need_weight and weight is not None) else O.new_empty(0)]
+
+
+def _mse_setup(ctx, inputs, output):
+    O, lse, target, weight, z, reduction = inputs
+    ctx.save_for_backward(O, lse, target, weight, output[1])
+    ctx.args = (z, reduction)
+
+
+def _mse_backward(ctx, grad, _grad_stats):
+    O, lse, target, weight, stats = ctx.saved_tensors
+    z, reduction = ctx.args
+    need_t = bool(ctx.needs_input_grad[2])
+    need_w = bool(ctx.needs_input_grad[3]) and weight is not None
+    if grad is None:
+        grad = torch.zeros(O.shape[0] if reduction == nat.REDUCE_NONE else (), dtype=O.dtype, device=O.device)
+    gO, glse, gt, gw = _mse_bwd_op(grad, O, lse, target, weight, stats, z, reduction, need_t, need_w)
+    return gO, glse, (gt if need_t else None), (gw if need_w else None), None, None
+
+
+_mse_op.register_autograd(_mse_backward, setup_context=_mse_setup)
+
+
+def mse_loss_op(O, lse, target, weight, z_loss_weight, reduction: str):
+    """The loss epilogue of swvr/api.py:54-66 on ``O [N, D]``, ``lse [N]``."""
+    if reduction not in _REDUCTIONS:
+        raise ValueError(f"unknown reduction {reduction!r}")
+    N, D = O.shape
+    t = target.to(O.dtype).reshape(N, D).contiguous()
+    w = weight.to(O.dtype).reshape(N).contiguous() if weight is not None else None
+    with torch.autocast(O.device.type, enabled=False):
+        loss, _ = _mse_op(O, lse, t, w, float(z_loss_weight), _REDUCTIONS[reduction])
+    return loss

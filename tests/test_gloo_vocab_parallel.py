@@ -1,0 +1,134 @@
+"""Vocabulary-parallel collective logic on CPU gloo ranks (world size 2 and 3).
+
+The per-shard compute is the numpy oracle injected through ``vocab_parallel.set_backend``
+(the CUDA kernels need a GPU); everything else -- shard ranges, the all-gather of the
+online-softmax states, the rank-ordered merge, the dh all-reduce and the autograd wiring --
+is the production code.  Checked against the unsharded oracle.  A second test kills one
+rank before the collective and checks that the survivor fails with an error within the
+process-group timeout instead of hanging.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import swvr_oracle as orc
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class OracleBackend:
+    """numpy oracle standing in for the CUDA kernels on CPU ranks (fp64)."""
+
+    @staticmethod
+    def partial(h, W, E, bias, scale, chunk, cdt):
+        b = None if bias is None else bias.detach().numpy()
+        m2, l, acc = orc.shard_partials(h.detach().numpy(), W.detach().numpy(), E.detach().numpy(), b, scale, 1)
+        return torch.from_numpy(m2[0]), torch.from_numpy(l[0]), torch.from_numpy(acc[0])
+
+    @staticmethod
+    def combine(m2s, ls, accs):
+        O, lse = orc.combine_partials(m2s.numpy(), ls.numpy(), accs.numpy())
+        return torch.from_numpy(O), torch.from_numpy(lse)
+
+    @staticmethod
+    def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_W, need_E, need_b):
+        b = None if bias is None else bias.detach().numpy()
+        gh, gW, gE, gb = orc.chunked_backward(gO.numpy(), glse.numpy(), h.detach().numpy(), W.detach().numpy(),
+                                              E.detach().numpy(), b, O.numpy(), lse.numpy(), scale, chunk, "fp64",
+                                              True, need_W, need_E, need_b)
+        t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x))
+        return t(gh), t(gW), t(gE), t(gb)
+
+
+def _inputs(N=7, K=12, V=41, D=5):
+    g = torch.Generator().manual_seed(0)
+    h, W, E, b = (torch.randn(*s, generator=g, dtype=torch.float64) for s in ((N, K), (V, K), (V, D), (V,)))
+    gO = torch.randn(N, D, generator=g, dtype=torch.float64)
+    glse = torch.randn(N, generator=g, dtype=torch.float64)
+    return h, W, E, b, gO, glse
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    from swvr_b200 import vocab_parallel as vp
+    vp.set_backend(OracleBackend)
+    h, W, E, b, gO, glse = _inputs()
+    v0, v1 = vp.shard_range(W.shape[0], world, rank)
+    h = h.clone().requires_grad_(True)
+    Ws, Es, bs = (x[v0:v1].clone().requires_grad_(True) for x in (W, E, b))
+    O, lse = vp.softmax_readout_vocab_parallel(h, Ws, Es, bs, logit_scale=0.5, chunk_size=8)
+    ((O * gO).sum() + (lse * glse).sum()).backward()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), O=O.detach().numpy(), lse=lse.detach().numpy(),
+             gh=h.grad.numpy(), gW=Ws.grad.numpy(), gE=Es.grad.numpy(), gb=bs.grad.numpy(), v0=v0, v1=v1)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_parallel_matches_unsharded(tmp_path, world):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    h, W, E, b, gO, glse = (x.numpy() for x in _inputs())
+    O_ref, lse_ref = orc.softmax_readout_reference(h, W, E, b, 0.5)
+    gh, gW, gE, gb = orc.readout_grads(h, W, E, b, gO, glse, 0.5)
+    outs = [dict(np.load(tmp_path / f"rank{r}.npz")) for r in range(world)]
+    covered = 0
+    for r, o in enumerate(outs):
+        # O and LSE are identical on every rank (same rank-ordered merge)
+        np.testing.assert_array_equal(o["O"], outs[0]["O"])
+        np.testing.assert_allclose(o["O"], O_ref, rtol=1e-12, atol=1e-14)
+        np.testing.assert_allclose(o["lse"], lse_ref, rtol=1e-12)
+        np.testing.assert_allclose(o["gh"], gh, rtol=1e-10, atol=1e-13)
+        v0, v1 = int(o["v0"]), int(o["v1"])
+        np.testing.assert_allclose(o["gW"], gW[v0:v1], rtol=1e-10, atol=1e-13)
+        np.testing.assert_allclose(o["gE"], gE[v0:v1], rtol=1e-10, atol=1e-13)
+        np.testing.assert_allclose(o["gb"], gb[v0:v1], rtol=1e-10, atol=1e-13)
+        assert v0 == covered
+        covered = v1
+    assert covered == W.shape[0]
+
+
+def _failing_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from swvr_b200 import vocab_parallel as vp
+    vp.set_backend(OracleBackend)
+    h, W, E, b, _, _ = _inputs()
+    if rank == 1:
+        # this rank dies between steps, before its collective: no exit handshake
+        os._exit(3)
+    v0, v1 = vp.shard_range(W.shape[0], world, rank)
+    try:
+        vp.softmax_readout_vocab_parallel(h, W[v0:v1], E[v0:v1], b[v0:v1])
+        status = "completed"
+    except Exception as exc:  # the all-gather must fail, not hang
+        status = f"raised {type(exc).__name__}"
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(status)
+    os._exit(0)
+
+
+def test_dead_rank_is_detected_by_timeout(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung instead of failing"
+    assert procs[1].exitcode == 3
+    status = (tmp_path / "rank0.txt").read_text()
+    assert status.startswith("raised"), status
