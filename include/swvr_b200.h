@@ -140,9 +140,12 @@ int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t
  *   per_tok = mean_d (O - target)^2 + z_loss_weight * LSE^2, times weight[n] if weight;
  *   NONE -> out [N]; SUM -> out [1] = sum; MEAN -> out [1] = sum / (sum(weight) or N).
  * O, lse, target, weight (may be NULL), out and stats share `dtype` (F32 or F64).  For SUM and
- * MEAN one CUDA block reduces in a fixed order (deterministic) and, when stats is not NULL,
- * writes stats[0] = sum_n weight[n] * per_tok[n] and stats[1] = the denominator (1 for SUM).
+ * MEAN the reduction runs over a fixed grid in a fixed order (deterministic) and needs
+ * `stats`, an array of SWVR_MSE_STATS_LEN elements: on return stats[0] = sum_n weight[n] *
+ * per_tok[n] and stats[1] = the denominator (1 for SUM); the rest is scratch.
  */
+#define SWVR_MSE_STATS_LEN 514
+
 int swvr_mse_fwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,
                  const void* target, const void* weight, double z_loss_weight, int32_t reduction, void* out,
                  void* stats, void* stream);

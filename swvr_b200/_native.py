@@ -20,6 +20,7 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, -1, -2, -3, -4
 F32, F64, BF16, F16 = 0, 1, 2, 3
 REDUCE_NONE, REDUCE_SUM, REDUCE_MEAN = 0, 1, 2
+MSE_STATS_LEN = 514  # SWVR_MSE_STATS_LEN
 
 DTYPE_CODE = {torch.float32: F32, torch.float64: F64, torch.bfloat16: BF16, torch.float16: F16}
 

@@ -394,6 +394,13 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     sp.ld_ds = b.Npad;
     sp.part_de = part_de;
     sp.part_db = part_db;
+    if (b.need_ds) {
+      SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
+      SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
+      sm.ds = gm.ds_k;
+    } else {
+      sm.ds = sm.go;  // unused
+    }
     {
       ProfScope ps(kProfBwdScores, st);
       SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, std::min(sp.units, b.sms), st));
@@ -405,8 +412,6 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
                                     g.grad_E_dtype, g.ld_grad_E, g.grad_bias, g.grad_bias_dtype, st));
     }
     if (b.need_ds) {
-      SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
-      SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
       tc::GemmParams gp{};
       const int nt = static_cast<int>(ceil_div(K, 256));
       gp.dw_mt = VTc;
@@ -563,6 +568,8 @@ int swvr_mse_fwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void*
   if (reduction < SWVR_REDUCE_NONE || reduction > SWVR_REDUCE_MEAN)
     return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown reduction %d", reduction);
   if (!out || (n_tokens > 0 && (!O || !lse || !target))) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (reduction != SWVR_REDUCE_NONE && !stats)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "SUM / MEAN need stats (SWVR_MSE_STATS_LEN elements)");
   ProfScope ps(kProfMse, static_cast<cudaStream_t>(stream));
   SWVR_CUDA(small::mse_fwd(dtype, n_tokens, embed_dim, O, lse, target, weight, z, reduction, out, stats,
                            static_cast<cudaStream_t>(stream)));

@@ -181,14 +181,19 @@ __global__ void mse_none_kernel(int64_t N, int64_t D, const T* O, const T* lse, 
   if (threadIdx.x % 32 == 0) out[n] = w ? raw * w[n] : raw;
 }
 
-// One block, fixed summation order: out[0] = loss; stats[0] = sum(w * raw), stats[1] = denom.
+// Deterministic two-stage reduction over a fixed grid of kMseBlocks blocks (one warp per
+// row, rows assigned round-robin in a fixed pattern): stage 1 writes each block's
+// (sum w*raw, sum w) to stats[2 + 2b]; stage 2 (one block) adds them in block order and
+// writes out[0] = loss, stats[0] = sum(w * raw), stats[1] = denominator.
+constexpr int kMseBlocks = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(1024) mse_reduce_kernel(int64_t N, int64_t D, const T* O, const T* lse, const T* t,
-                                                          const T* w, T z, int reduction, T* out, T* stats) {
-  __shared__ T sh_s[32], sh_w[32];
+__global__ void __launch_bounds__(256) mse_partial_kernel(int64_t N, int64_t D, const T* O, const T* lse, const T* t,
+                                                          const T* w, T z, T* stats) {
+  __shared__ T sh_s[8], sh_w[8];
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   T s = 0, ws = 0;
-  for (int64_t n = warp; n < N; n += 32) {
+  for (int64_t n = static_cast<int64_t>(blockIdx.x) * 8 + warp; n < N; n += static_cast<int64_t>(kMseBlocks) * 8) {
     const T raw = row_raw<T>(O, t, lse, n, D, z, lane);
     const T wn = w ? w[n] : T(1);
     s += raw * wn;
@@ -201,17 +206,34 @@ __global__ void __launch_bounds__(1024) mse_reduce_kernel(int64_t N, int64_t D, 
   __syncthreads();
   if (threadIdx.x == 0) {
     T S = 0, Wt = 0;
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 8; ++i) {
       S += sh_s[i];
       Wt += sh_w[i];
     }
-    T denom = T(1);
-    if (reduction == SWVR_REDUCE_MEAN) denom = w ? Wt : static_cast<T>(N);
-    out[0] = S / denom;
-    if (stats) {
-      stats[0] = S;
-      stats[1] = denom;
+    stats[2 + 2 * blockIdx.x] = S;
+    stats[3 + 2 * blockIdx.x] = Wt;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) mse_final_kernel(int64_t N, int reduction, bool weighted, T* out, T* stats) {
+  __shared__ T sh_s[kMseBlocks], sh_w[kMseBlocks];
+  sh_s[threadIdx.x] = stats[2 + 2 * threadIdx.x];
+  sh_w[threadIdx.x] = stats[3 + 2 * threadIdx.x];
+  __syncthreads();
+  for (int stride = kMseBlocks / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) {
+      sh_s[threadIdx.x] += sh_s[threadIdx.x + stride];
+      sh_w[threadIdx.x] += sh_w[threadIdx.x + stride];
     }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    T denom = T(1);
+    if (reduction == SWVR_REDUCE_MEAN) denom = weighted ? sh_w[0] : static_cast<T>(N);
+    out[0] = sh_s[0] / denom;
+    stats[0] = sh_s[0];
+    stats[1] = denom;
   }
 }
 
@@ -252,9 +274,10 @@ static cudaError_t mse_fwd_t(int64_t N, int64_t D, const void* O, const void* ls
         N, D, static_cast<const T*>(O), static_cast<const T*>(lse), static_cast<const T*>(t),
         static_cast<const T*>(w), static_cast<T>(z), static_cast<T*>(out));
   } else {
-    mse_reduce_kernel<T><<<1, 1024, 0, st>>>(N, D, static_cast<const T*>(O), static_cast<const T*>(lse),
-                                              static_cast<const T*>(t), static_cast<const T*>(w), static_cast<T>(z),
-                                              red, static_cast<T*>(out), static_cast<T*>(stats));
+    mse_partial_kernel<T><<<kMseBlocks, 256, 0, st>>>(N, D, static_cast<const T*>(O), static_cast<const T*>(lse),
+                                                      static_cast<const T*>(t), static_cast<const T*>(w),
+                                                      static_cast<T>(z), static_cast<T*>(stats));
+    mse_final_kernel<T><<<1, kMseBlocks, 0, st>>>(N, red, w != nullptr, static_cast<T*>(out), static_cast<T*>(stats));
   }
   return cudaGetLastError();
 }

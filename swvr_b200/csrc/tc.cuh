@@ -46,7 +46,7 @@ struct BwdScoresParams {
 };
 
 struct BwdScoresMaps {
-  CUtensorMap w, h, e, go;
+  CUtensorMap w, h, e, go, ds;  // ds: this chunk's dS^T [rows, Npad], box {64, 128} (TMA store)
 };
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,

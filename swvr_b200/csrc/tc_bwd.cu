@@ -29,7 +29,8 @@ struct BwdCfg {
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
   static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
   static constexpr int SMEM_GO = SMEM_E + E_BYTES;
-  static constexpr int SMEM_LSE = SMEM_GO + 2 * GO_BYTES;
+  static constexpr int SMEM_STG = SMEM_GO + 2 * GO_BYTES;  // dS tile staging: two 128 x 64 boxes
+  static constexpr int SMEM_LSE = SMEM_STG + 2 * BOX;
   static constexpr int SMEM_DELTA = SMEM_LSE + 512;
   static constexpr int SMEM_BAR = SMEM_DELTA + 512;
   static constexpr int NBAR = 2 * NS + 13;
@@ -44,7 +45,7 @@ template <bool kBF16, int DP, int NS>
 __global__ void __launch_bounds__(256, 1)
     bwd_scores_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_h,
                       const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_go,
-                      const BwdScoresParams p) {
+                      const __grid_constant__ CUtensorMap tm_ds, const BwdScoresParams p) {
   using Cfg = BwdCfg<kBF16, DP, NS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(256, 1)
     tma_prefetch_desc(&tm_h);
     tma_prefetch_desc(&tm_e);
     tma_prefetch_desc(&tm_go);
+    if (p.ds) tma_prefetch_desc(&tm_ds);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -210,8 +212,13 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // -------------------------------------------------------------- gradient warps
+    // lse_s holds -LSE*log2e and delta_s holds -delta for the current token tile, so each
+    // pair of tokens costs a handful of packed f32x2 ops.  dS*s goes to a 128B-swizzled
+    // staging tile that one thread stores with two TMA bulk copies per token tile.
     const int r = threadIdx.x - 128;
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    uint8_t* stg = smem + Cfg::SMEM_STG;
+    const float2 sc2v = make_float2(p.sc2, p.sc2), scalev = make_float2(p.scale, p.scale);
     uint32_t g = 0, uc = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
       const int vt = u / p.TS, ts = u % p.TS;
@@ -220,14 +227,17 @@ __global__ void __launch_bounds__(256, 1)
       const int vrow = p.v_begin + vt * 128 + r;
       const bool vvalid = vrow < p.v_end;
       const float b2 = (p.bias != nullptr && vvalid) ? load_f(p.bias, p.bias_dt, vrow) * kLog2e : 0.f;
-      float db = 0.f;
+      const float2 b2v = make_float2(b2, b2);
+      float2 db = make_float2(0.f, 0.f);
       for (int it = it0; it < it1; ++it, ++g) {
         const int t0 = it * 128;
+        // the previous tile's dS store must have finished reading the staging tile
+        if (need_ds && r == 0) tma_store_wait_read<0>();
         named_bar_sync(1, 128);
         {
           const int t = t0 + r;
-          lse_s[r] = t < p.N ? p.lse[t] * kLog2e : INFINITY;
-          delta_s[r] = t < p.N ? p.delta[t] : 0.f;
+          lse_s[r] = t < p.N ? -p.lse[t] * kLog2e : -INFINITY;
+          delta_s[r] = t < p.N ? -p.delta[t] : 0.f;
         }
         named_bar_sync(1, 128);
         const uint32_t b = g & 1u;
@@ -242,24 +252,47 @@ __global__ void __launch_bounds__(256, 1)
           tmem_ld32(trow + Cfg::DP_COL + c * 32, dp);
           tmem_wait_ld();
           uint32_t pk_p[16], pk_ds[16];
+          const float4* L4 = reinterpret_cast<const float4*>(lse_s + c * 32);
+          const float4* D4 = reinterpret_cast<const float4*>(delta_s + c * 32);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int tt = c * 32 + i;
-            const float p0 = ex2(fmaf(__uint_as_float(s[i]), p.sc2, b2) - lse_s[tt]);
-            const float p1 = ex2(fmaf(__uint_as_float(s[i + 1]), p.sc2, b2) - lse_s[tt + 1]);
-            const float d0 = p0 * (__uint_as_float(dp[i]) - delta_s[tt]);
-            const float d1 = p1 * (__uint_as_float(dp[i + 1]) - delta_s[tt + 1]);
-            db += d0 + d1;
-            pk_ds[i / 2] = pack2<kBF16>(d0 * p.scale, d1 * p.scale);
-            pk_p[i / 2] = pack2<kBF16>(p0, p1);
+          for (int q = 0; q < 8; ++q) {
+            const float4 nl = L4[q], nd = D4[q];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int i = 4 * q + 2 * hh;
+              const float2 sv = make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+              const float2 dpv = make_float2(__uint_as_float(dp[i]), __uint_as_float(dp[i + 1]));
+              const float2 bl = fadd2(b2v, hh ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y));
+              const float2 x = ffma2(sv, sc2v, bl);
+              const float2 pv = make_float2(ex2(x.x), ex2(x.y));
+              const float2 d = fmul2(pv, fadd2(dpv, hh ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y)));
+              db = fadd2(db, d);
+              const float2 dsv = fmul2(d, scalev);
+              pk_ds[i / 2] = pack2<kBF16>(dsv.x, dsv.y);
+              pk_p[i / 2] = pack2<kBF16>(pv.x, pv.y);
+            }
           }
-          if (need_ds && vvalid) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.ds) +
-                                                  static_cast<int64_t>(vrow - p.v_begin) * p.ld_ds + t0 + c * 32);
+          if (need_ds) {
+            // tokens [32c, 32c + 32) of row r: box c/2, 16-byte chunks (c%2)*4 + q, 128B swizzle
+            uint8_t* row = stg + (c >> 1) * Cfg::BOX + r * 128;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
+            for (int q = 0; q < 4; ++q) {
+              const int j = (c & 1) * 4 + q;
+              *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
+                  make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
+            }
           }
           if (need_de) tmem_st16(sbase + c * 16, pk_p);
+        }
+        if (need_ds) {
+          fence_proxy_async_smem();
+          named_bar_sync(1, 128);
+          if (r == 0) {
+            const int row0 = vt * 128;
+            tma_store_2d(&tm_ds, stg, t0, row0);
+            tma_store_2d(&tm_ds, stg + Cfg::BOX, t0 + 64, row0);
+            tma_store_commit();
+          }
         }
         if (need_de) tmem_wait_st();
         tc_fence_before();
@@ -285,9 +318,10 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_before();
         mbar_arrive(de_free);
       }
-      if (need_db && vvalid) p.part_db[slot] = db;
+      if (need_db && vvalid) p.part_db[slot] = db.x + db.y;
       ++uc;
     }
+    if (need_ds && r == 0) tma_store_wait_all<0>();
   }
 done:
   tc_fence_before();
@@ -305,14 +339,14 @@ static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm
   auto kern = bwd_scores_kernel<kBF16, DP, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
-  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(m.w, m.h, m.e, m.go, prm);
+  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(m.w, m.h, m.e, m.go, m.ds, prm);
   return cudaGetLastError();
 }
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
                                      int grid, cudaStream_t st) {
   if (DP == 64) return bf16 ? launch_bwd<true, 64, 4>(maps, prm, grid, st) : launch_bwd<false, 64, 4>(maps, prm, grid, st);
-  return bf16 ? launch_bwd<true, 128, 4>(maps, prm, grid, st) : launch_bwd<false, 128, 4>(maps, prm, grid, st);
+  return bf16 ? launch_bwd<true, 128, 3>(maps, prm, grid, st) : launch_bwd<false, 128, 3>(maps, prm, grid, st);
 }
 
 }  // namespace tc

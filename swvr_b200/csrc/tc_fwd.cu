@@ -34,8 +34,10 @@ struct FwdCfg {
   static constexpr int SMEM_A = 0;
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
   static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
-  static constexpr int SMEM_BAR = SMEM_E + 2 * E_BYTES;
+  static constexpr int SMEM_BIAS = SMEM_E + 2 * E_BYTES;  // 2 x 256 floats: bias*log2e, -inf past V
+  static constexpr int SMEM_BAR = SMEM_BIAS + 2 * 256 * 4;
   static constexpr int NBAR = 2 * NS + 11;  // last one: abort drain
+  static constexpr float kEmergency = kBF16 ? 64.f : 8.f;  // max P = 2^kEmergency stays finite in 16 bits
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
   static constexpr uint32_t O_COL = 2 * BV;
@@ -44,11 +46,6 @@ struct FwdCfg {
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0 && E_BOX % 1024 == 0, "1024-byte alignment");
 };
-
-__device__ __forceinline__ float bias2_at(const FwdParams& p, int col) {
-  if (p.bias == nullptr || col >= p.V) return 0.f;
-  return load_f(p.bias, p.bias_dt, col) * kLog2e;
-}
 
 template <bool kBF16, int BV, int DP, int NS>
 __global__ void __launch_bounds__(256, 1)
@@ -184,79 +181,108 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // -------------------------------------------------------------- softmax warps
+    // One pass per tile.  P = 2^(t - ref) with t = S*s*log2e + b*log2e and ref an integer
+    // reference max (so every rescale factor is an exact power of two).  A 32-column chunk
+    // whose max exceeds ref + kEmergency raises ref to ceil(max) and rescales the P chunks
+    // of this tile already in TMEM, l, and (after the previous P.E completed) O.
     const int r = threadIdx.x - 128;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t trow = tmem + lane_base;
+    float* bias_s = reinterpret_cast<float*>(smem + Cfg::SMEM_BIAS);
     uint32_t g = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
       const int mt = u / p.splits, sp = u % p.splits;
       const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
       if (vt1 <= vt0) continue;
       const int n = mt * 128 + r;
-      float m2 = -INFINITY, l = 0.f;
+      float ref = -INFINITY, l = 0.f;
       for (int vt = vt0; vt < vt1; ++vt, ++g) {
         const uint32_t b = g & 1u;
         const bool not_first = vt > vt0;
+        const int v0 = vt * BV;
+        // stage this tile's bias (log2 units); columns past V get -inf, which masks them
+        float* bt = bias_s + b * 256;
+        for (int c = r; c < BV; c += 128) {
+          const int col = v0 + c;
+          bt[c] = col < p.V ? (p.bias ? load_f(p.bias, p.bias_dt, col) * kLog2e : 0.f) : -INFINITY;
+        }
+        named_bar_sync(1, 128);
         if (!warp_wait(&s_full[b], (g >> 1) & 1u, abort_flag, kErrFwd | 7)) goto done;
         tc_fence_after();
         const uint32_t sbase = trow + b * BV;
-        const int v0 = vt * BV;
-        // pass 1: row max of this tile (log2 units)
-        float mx = -INFINITY;
+        const float ref_start = ref;
+        float2 lsum = make_float2(0.f, 0.f);
 #pragma unroll 1
         for (int c = 0; c < BV / 32; ++c) {
           uint32_t x[32];
           tmem_ld32(sbase + c * 32, x);
           tmem_wait_ld();
+          float t[32];
+          const float4* b4 = reinterpret_cast<const float4*>(bt + c * 32);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = v0 + c * 32 + i;
-            const float t = col < p.V ? fmaf(__uint_as_float(x[i]), p.sc2, bias2_at(p, col)) : -INFINITY;
-            mx = fmaxf(mx, t);
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = b4[q];
+            const float2 t0 = ffma2(make_float2(__uint_as_float(x[4 * q]), __uint_as_float(x[4 * q + 1])),
+                                    make_float2(p.sc2, p.sc2), make_float2(bb.x, bb.y));
+            const float2 t1 = ffma2(make_float2(__uint_as_float(x[4 * q + 2]), __uint_as_float(x[4 * q + 3])),
+                                    make_float2(p.sc2, p.sc2), make_float2(bb.z, bb.w));
+            t[4 * q] = t0.x;
+            t[4 * q + 1] = t0.y;
+            t[4 * q + 2] = t1.x;
+            t[4 * q + 3] = t1.y;
           }
-        }
-        // the previous tile's P.E must be done before O is touched (consumes one completion)
-        if (not_first) {
-          if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 8)) goto done;
-          tc_fence_after();
-        }
-        const bool resc = mx > m2 + 8.f;
-        float alpha = 1.f;
-        if (resc) {
-          alpha = ex2(m2 - mx);
-          m2 = mx;
-          l *= alpha;
-        }
-        if (not_first && __any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-          for (int c = 0; c < DP / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(trow + Cfg::O_COL + c * 32, o);
-            tmem_wait_ld();
+          float cm = t[0];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(trow + Cfg::O_COL + c * 32, o);
-          }
-          tmem_wait_st();
-        }
-        const float ref = (m2 == -INFINITY) ? 0.f : m2;
-        // pass 2: P = 2^(t - ref), row sum, P (16-bit) back into TMEM over S
+          for (int i = 1; i < 32; ++i) cm = fmaxf(cm, t[i]);
+          const bool emerg = cm > ref + Cfg::kEmergency;
+          if (__any_sync(0xffffffffu, emerg)) {
+            const float newref = emerg ? cm : ref;
+            const float alpha = newref == ref ? 1.f : ex2(ref - newref);
+            if (c > 0) {
+              // rescale this tile's P chunks already written (16-bit pairs, exact power-of-two factor)
 #pragma unroll 1
-        for (int c = 0; c < BV / 32; ++c) {
-          uint32_t x[32];
-          tmem_ld32(sbase + c * 32, x);
-          tmem_wait_ld();
+              for (int cc = 0; cc < c; ++cc) {
+                uint32_t pk[16];
+                tmem_ld16(sbase + cc * 16, pk);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) pk[i] = scale2<kBF16>(pk[i], alpha);
+                tmem_st16(sbase + cc * 16, pk);
+              }
+              tmem_wait_st();
+            }
+            l *= alpha;
+            lsum.x *= alpha;
+            lsum.y *= alpha;
+            ref = newref;
+          }
+          const float refe = ref == -INFINITY ? 0.f : ref;
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const int col = v0 + c * 32 + i;
-            const float t0 = col < p.V ? fmaf(__uint_as_float(x[i]), p.sc2, bias2_at(p, col)) : -INFINITY;
-            const float t1 = col + 1 < p.V ? fmaf(__uint_as_float(x[i + 1]), p.sc2, bias2_at(p, col + 1)) : -INFINITY;
-            const float p0 = ex2(t0 - ref), p1 = ex2(t1 - ref);
-            l += p0 + p1;
+            const float p0 = ex2(t[i] - refe), p1 = ex2(t[i + 1] - refe);
+            lsum = fadd2(lsum, make_float2(p0, p1));
             pk[i / 2] = pack2<kBF16>(p0, p1);
           }
           tmem_st16(sbase + c * 16, pk);
+        }
+        l += lsum.x + lsum.y;
+        // the previous tile's P.E must be done before O is rescaled (consumes one completion)
+        if (not_first) {
+          if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 8)) goto done;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, ref != ref_start)) {
+            const float alpha = ref == ref_start ? 1.f : ex2(ref_start - ref);
+#pragma unroll 1
+            for (int c = 0; c < DP / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(trow + Cfg::O_COL + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(trow + Cfg::O_COL + c * 32, o);
+            }
+          }
         }
         tmem_wait_st();
         tc_fence_before();
@@ -283,7 +309,7 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_before();
         mbar_arrive(o_free);
         if (n < p.N) {
-          p.part_m2[slot] = m2;
+          p.part_m2[slot] = ref;
           p.part_l[slot] = l;
         }
       }
@@ -317,7 +343,7 @@ cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdP
   if (DP == 64) {
     return bf16 ? launch_fwd<true, 192, 64, 4>(maps, prm, grid, st) : launch_fwd<false, 192, 64, 4>(maps, prm, grid, st);
   }
-  return bf16 ? launch_fwd<true, 160, 128, 4>(maps, prm, grid, st) : launch_fwd<false, 160, 128, 4>(maps, prm, grid, st);
+  return bf16 ? launch_fwd<true, 160, 128, 3>(maps, prm, grid, st) : launch_fwd<false, 160, 128, 3>(maps, prm, grid, st);
 }
 
 }  // namespace tc

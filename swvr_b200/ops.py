@@ -265,7 +265,7 @@ def _mse_op(O: torch.Tensor, lse: torch.Tensor, target: torch.Tensor, weight: Op
     dev = _require_cuda(O, lse, target, weight)
     N, D = O.shape
     out = torch.empty((N,) if reduction == nat.REDUCE_NONE else (), dtype=O.dtype, device=dev)
-    stats = torch.zeros(2, dtype=O.dtype, device=dev)
+    stats = torch.zeros(nat.MSE_STATS_LEN, dtype=O.dtype, device=dev)
     with torch.cuda.device(dev):
         nat.check(nat.lib().swvr_mse_fwd(N, D, nat.dtype_code(O.dtype), O.data_ptr(), lse.data_ptr(),
                                          target.data_ptr(), nat.ptr(weight), float(z_loss_weight), int(reduction),
@@ -276,7 +276,7 @@ def _mse_op(O: torch.Tensor, lse: torch.Tensor, target: torch.Tensor, weight: Op
 @_mse_op.register_fake
 def _(O, lse, target, weight, z_loss_weight, reduction):
     shape = (O.shape[0],) if reduction == nat.REDUCE_NONE else ()
-    return O.new_empty(shape), O.new_empty(2)
+    return O.new_empty(shape), O.new_empty(nat.MSE_STATS_LEN)
 
 
 @torch.library.custom_op("swvr_b200::mse_bwd", mutates_args=())

@@ -57,7 +57,10 @@ def functional_grads(fn, inputs, seed=1):
     g = torch.Generator().manual_seed(seed)
     ws = [torch.randn(o.shape, generator=g, dtype=f64).to(o) for o in outs]
     loss = sum((o * w).sum() for o, w in zip(outs, ws))
-    xs = [x for x in inputs if x is not None and x.requires_grad]
+    xs = []
+    for x in inputs:
+        if x is not None and x.requires_grad and all(x is not y for y in xs):
+            xs.append(x)
     return outs, ws, torch.autograd.grad(loss, xs, allow_unused=True)
 
 

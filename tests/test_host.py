@@ -116,7 +116,7 @@ def test_fake_impls_give_shapes(dtype, adt):
     grads = torch.ops.swvr_b200.bwd(O, lse, h, W, E, b, O, lse, 1.0, 8192, dtype, True, False, True, True)
     assert [tuple(g.shape) for g in grads] == [(6, 16), (0,), (100, 5), (100,)]
     loss, stats = torch.ops.swvr_b200.mse(O, lse, O, None, 0.0, 2)
-    assert loss.shape == () and stats.shape == (2,)
+    assert loss.shape == () and stats.shape == (nat.MSE_STATS_LEN,)
 
 
 def test_module_holds_references():
