@@ -91,6 +91,22 @@ int swvr_fwd_partial(const swvr_problem* p, void* m2, void* l, void* acc, void* 
                      void* stream);
 
 /*
+ * Forward without a workspace, for callers that cannot allocate device memory at call
+ * time: hosts that plan every byte of device memory up front and give plugins no
+ * allocator, or FFI hosts (cgo, JNI, N-API) that forbid their plugins cudaMalloc, which can
+ * synchronise the device and fragments a pool the host manages.  No counterpart in the
+ * reference.  Same inputs and outputs as swvr_fwd (bf16 / fp16 compute only); the kernel's
+ * scratch lives in a static device array of the library, 16 MiB on every GPU that loads the
+ * library, held until exit.  Problems whose scratch does not fit (about N * (D + 2) * 4 bytes
+ * when the vocabulary is not split, e.g. N = 16384 at D = 64 uses 4.3 MB) return
+ * SWVR_ERR_UNSUPPORTED with a message.  The first call on each device looks the array up
+ * (with that device current); make it before any stream capture.  All calls on a device
+ * share the array: calls that overlap on the GPU race and must be serialised by the caller.
+ * Allocates nothing: no cudaMalloc / cudaFree and no allocating library routine.
+ */
+int swvr_fwd_noalloc(const swvr_problem* p, void* O, void* lse, void* stream);
+
+/*
  * Merge `shards` partial states ([shards, N], [shards, N], [shards, N, D], shard-major,
  * contiguous) in shard order into O [N, D] and LSE [N].  Deterministic.  The same merge as
  * the chunk loop of chunked.py:96-105, applied across shards.

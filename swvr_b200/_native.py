@@ -68,6 +68,7 @@ _SIGNATURES = {
                              c_int32, c_void_p, c_void_p, c_void_p]),
     "swvr_mse_bwd": (c_int, [c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_double,
                              c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "swvr_fwd_noalloc": (c_int, [POINTER(Problem), c_void_p, c_void_p, c_void_p]),
     "swvr_profile_start": (c_int, []),
     "swvr_profile_stop": (c_int, [POINTER(ProfileRecord), c_int, POINTER(c_int)]),
 }

@@ -5,3 +5,4 @@
 #include "tc_bwd.cu"
 #include "tc_gemm.cu"
 #include "abi.cu"
+#include "noalloc.cu"
