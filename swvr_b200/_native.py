@@ -14,7 +14,8 @@ from ctypes import POINTER, c_char_p, c_double, c_int, c_int32, c_int64, c_size_
 import torch
 
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
-LIB_PATH = os.path.join(LIB_DIR, "libswvr_b200.so")
+# SWVR_LIB overrides the library file (e.g. an installed copy); default: the in-tree build.
+LIB_PATH = os.environ.get("SWVR_LIB") or os.path.join(LIB_DIR, "libswvr_b200.so")
 HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "swvr_b200.h")
 
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, -1, -2, -3, -4

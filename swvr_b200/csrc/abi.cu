@@ -277,8 +277,9 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   b.DP = p.embed_dim <= 64 ? 64 : 128;
   b.NT = static_cast<int>(ceil_div(p.n_tokens, 128));
   b.Npad = static_cast<int64_t>(b.NT) * 128;
-  int64_t C = round_up(std::max<int64_t>(p.chunk, 1), 128);
-  C = std::min<int64_t>(C, round_up(std::max<int64_t>(p.vocab, 1), 128));
+  // a multiple of 256 so that only the last chunk has a partial 256-row pair tile
+  int64_t C = round_up(std::max<int64_t>(p.chunk, 1), 256);
+  C = std::min<int64_t>(C, round_up(std::max<int64_t>(p.vocab, 1), 256));
   b.C = static_cast<int>(C);
   b.need_h = g.grad_h || g.grad_h_acc;
   b.need_W = g.grad_W != nullptr;
@@ -414,20 +415,20 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     if (b.need_ds) {
       tc::GemmParams gp{};
       const int nt = static_cast<int>(ceil_div(K, 256));
-      gp.dw_mt = VTc;
+      gp.dw_mt = static_cast<int>(ceil_div(rows, 256));
       gp.dw_nt = nt;
       gp.dw_kb = static_cast<int>(b.Npad / 64);
-      gp.dw_tiles = g.grad_W ? VTc * nt : 0;
-      gp.dh_mt = b.NT;
+      gp.dw_tiles = g.grad_W ? gp.dw_mt * nt : 0;
+      gp.dh_mt = static_cast<int>(ceil_div(b.Npad, 256));
       gp.dh_nt = nt;
       gp.dh_kb = static_cast<int>(ceil_div(rows, 64));
-      gp.dh_tiles = dh ? b.NT * nt : 0;
+      gp.dh_tiles = dh ? gp.dh_mt * nt : 0;
       gp.v_begin = static_cast<int>(v0);
       gp.gw_f32 = g.grad_W_dtype == SWVR_F32 ? 1 : 0;
       const int tiles = gp.dw_tiles + gp.dh_tiles;
       if (tiles > 0) {
         ProfScope ps(kProfGemm, st);
-        SWVR_CUDA(tc::launch_gemm_kernel(bf16, gm, gp, std::min(tiles, b.sms), st));
+        SWVR_CUDA(tc::launch_gemm_kernel(bf16, gm, gp, b.sms / 2, st));
       }
     }
   }

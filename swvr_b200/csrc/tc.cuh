@@ -54,9 +54,9 @@ cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& map
 
 // ------------------------------------------------------------------ backward: dW / dh GEMMs
 struct GemmParams {
-  int dw_tiles, dh_tiles;    // number of 128x256 output tiles of each problem
-  int dw_mt, dw_nt, dw_kb;   // dW: row tiles (chunk rows / 128), column tiles (K / 256), k-blocks (tokens / 64)
-  int dh_mt, dh_nt, dh_kb;   // dh: row tiles (tokens / 128), column tiles, k-blocks (chunk rows / 64)
+  int dw_tiles, dh_tiles;    // number of 256x256 pair tiles of each problem
+  int dw_mt, dw_nt, dw_kb;   // dW: row tiles (chunk rows / 256), column tiles (K / 256), k-blocks (tokens / 64)
+  int dh_mt, dh_nt, dh_kb;   // dh: row tiles (tokens / 256), column tiles, k-blocks (chunk rows / 64)
   int v_begin;               // first vocabulary row of the chunk
   int gw_f32;                // dW output is fp32 (else the 16-bit compute dtype)
 };
@@ -70,7 +70,9 @@ struct GemmMaps {
   CUtensorMap dh;     // fp32 dh accumulator (TMA reduce-add), box {32, 128}
 };
 
-cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int grid, cudaStream_t st);
+// Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
+cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs,
+                               cudaStream_t st);
 
 }  // namespace tc
 }  // namespace swvr

@@ -1,16 +1,24 @@
 // Tensor-core (tcgen05) GEMMs of the backward on sm_100a: for one vocabulary chunk,
 //   dW_c = dS_c^T . h        (M = chunk rows, N = hidden, K = tokens)    -> gW rows
 //   dh  += dS_c   . W_c      (M = tokens, N = hidden, K = chunk rows)    -> fp32 accumulator
-// from the dS^T chunk that bwd_scores_kernel wrote.  Both problems share one persistent
-// launch (dW tiles first, then dh tiles; each CTA takes tiles round-robin) with 128 x 256
-// output tiles, a 4-stage TMA ring of 128B-swizzled tiles, and two TMEM accumulators so the
-// epilogue of one tile overlaps the main loop of the next.  The epilogue stages 128-byte
-// row slabs in shared memory and writes them with TMA: a store for dW (cast to the W
-// dtype) and an element-wise TMA add-reduction into the fp32 dh accumulator, so dh is
-// never read back into the SM.  Chunks run in order, so dh's accumulation order is fixed.
+// from the dS^T chunk that bwd_scores_kernel wrote.
+//
+// 2-SM design: CTA pairs (clusters of 2) compute 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2.  Each CTA of a pair stages its own 128 rows of A and its own
+// 128-column half of B per K-block (32 KB instead of 48 KB for a single-CTA 128 x 256
+// tile), so shared-memory traffic per FLOP drops by a third.  The even CTA (the leader)
+// issues every MMA; its commits arrive on the barriers of both CTAs, and both CTAs' TMA
+// loads count their bytes on the leader's barrier.  Each CTA's epilogue reads its own 128
+// rows from its TMEM and writes them with TMA: a store for dW (cast to the W dtype) and an
+// element-wise TMA add-reduction into the fp32 dh accumulator.  Both problems share one
+// persistent launch (dW tiles first); chunks run in order, so dh's accumulation order is
+// fixed.
 //
 // Replaces the reference's cuBLAS calls gH += mm_acc(gS, W_c) and gW[v0:v1] = mm_acc(gS^T, h)
 // (swvr/chunked.py:146-150).
+#include <cstdio>
+#include <cstdlib>
+
 #include "ptx.cuh"
 #include "tc.cuh"
 
@@ -19,8 +27,8 @@ namespace tc {
 
 template <int NS>
 struct GemmCfg {
-  static constexpr int A_BYTES = 128 * 128;  // 128 rows x 64 16-bit elements
-  static constexpr int B_BYTES = 256 * 128;  // 4 boxes of 64 rows x 64 elements
+  static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 64 16-bit elements
+  static constexpr int B_BYTES = 128 * 128;  // this CTA's 128 columns: two 64 x 64 boxes
   static constexpr int BOX64 = 64 * 128;     // one 64 x 64 box
   static constexpr int STG_BYTES = 128 * 128;
   static constexpr int SMEM_A = 0;
@@ -38,6 +46,7 @@ struct TileInfo {
   int mb, nb, kblocks;
 };
 
+// Pair tiles: dW tiles first (mb over 256-row blocks of the chunk), then dh tiles.
 __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   TileInfo ti;
   if (t < p.dw_tiles) {
@@ -74,15 +83,18 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + NS;
-  uint64_t* acc_full = bars + 2 * NS;  // [2]
-  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* full = bars;               // [NS] leader's copy counts both CTAs' bytes
+  uint64_t* empty = bars + NS;         // [NS] both CTAs (multicast commit)
+  uint64_t* acc_full = bars + 2 * NS;  // [2]  both CTAs (multicast commit)
+  uint64_t* acc_empty = acc_full + 2;  // [2]  leader's copy: one arrival per CTA
   uint64_t* spare = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles = p.dw_tiles + p.dh_tiles;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -91,7 +103,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 2);
     }
     mbar_init(spare, 1);
     *abort_flag = 0;
@@ -106,37 +118,38 @@ __global__ void __launch_bounds__(256, 1)
     tma_prefetch_desc(&tm_dh);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_holder, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
+      // ------------------------------------------------------------ TMA producer (both CTAs)
       uint32_t stage = 0, sphase = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      for (int t = pair; t < ntiles; t += npairs) {
         const TileInfo ti = decode_tile(p, t);
+        const int row = ti.mb * 256 + static_cast<int>(rank) * 128;
+        const int col = ti.nb * 256 + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < ti.kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrGemm | 1)) goto done;
-          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
           uint8_t* a = smem + Cfg::SMEM_A + stage * Cfg::A_BYTES;
           uint8_t* b = smem + Cfg::SMEM_B + stage * Cfg::B_BYTES;
           if (ti.dw) {
-            tma_load_2d(a, &tm_ds_k, &full[stage], kb * 64, ti.mb * 128);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tma_load_2d(b + c * Cfg::BOX64, &tm_h_mn, &full[stage], ti.nb * 256 + c * 64, kb * 64);
+            tma_load_2d_pair(a, &tm_ds_k, fb, kb * 64, row);
+            tma_load_2d_pair(b, &tm_h_mn, fb, col, kb * 64);
+            tma_load_2d_pair(b + Cfg::BOX64, &tm_h_mn, fb, col + 64, kb * 64);
           } else {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-              tma_load_2d(a + c * Cfg::BOX64, &tm_ds_mn, &full[stage], ti.mb * 128 + c * 64, kb * 64);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tma_load_2d(b + c * Cfg::BOX64, &tm_w_mn, &full[stage], ti.nb * 256 + c * 64, p.v_begin + kb * 64);
+            tma_load_2d_pair(a, &tm_ds_mn, fb, row, kb * 64);
+            tma_load_2d_pair(a + Cfg::BOX64, &tm_ds_mn, fb, row + 64, kb * 64);
+            tma_load_2d_pair(b, &tm_w_mn, fb, col, p.v_begin + kb * 64);
+            tma_load_2d_pair(b + Cfg::BOX64, &tm_w_mn, fb, col + 64, p.v_begin + kb * 64);
           }
           if (++stage == NS) {
             stage = 0;
@@ -146,12 +159,12 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      const uint32_t id_dw = idesc_f16(kBF16, 128, 256, false, true);
-      const uint32_t id_dh = idesc_f16(kBF16, 128, 256, true, true);
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      const uint32_t id_dw = idesc_f16(kBF16, 256, 256, false, true);
+      const uint32_t id_dh = idesc_f16(kBF16, 256, 256, true, true);
       uint32_t stage = 0, sphase = 0, tc = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      for (int t = pair; t < ntiles; t += npairs, ++tc) {
         const TileInfo ti = decode_tile(p, t);
         const uint32_t ab = tc & 1u;
         if (!mbar_wait(&acc_empty[ab], ((tc >> 1) & 1u) ^ 1u, abort_flag, kErrGemm | 2)) goto done;
@@ -166,28 +179,29 @@ __global__ void __launch_bounds__(256, 1)
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t bdesc = sdesc_sw128(bbase + ks * 2048, Cfg::BOX64, 1024);
             if (ti.dw)
-              umma_ss(dcol, sdesc_sw128(abase + ks * 32, 16, 1024), bdesc, id_dw, (kb | ks) ? 1u : 0u);
+              umma2_ss(dcol, sdesc_sw128(abase + ks * 32, 16, 1024), bdesc, id_dw, (kb | ks) ? 1u : 0u);
             else
-              umma_ss(dcol, sdesc_sw128(abase + ks * 2048, Cfg::BOX64, 1024), bdesc, id_dh, (kb | ks) ? 1u : 0u);
+              umma2_ss(dcol, sdesc_sw128(abase + ks * 2048, Cfg::BOX64, 1024), bdesc, id_dh, (kb | ks) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          umma2_commit_mc(&empty[stage], 3);
           if (++stage == NS) {
             stage = 0;
             sphase ^= 1u;
           }
         }
-        umma_commit(&acc_full[ab]);
+        umma2_commit_mc(&acc_full[ab], 3);
       }
     }
   } else if (warp >= 4) {
-    // -------------------------------------------------------------- epilogue warps
+    // -------------------------------------------------------------- epilogue warps (both CTAs)
     const int r = threadIdx.x - 128;
-    const bool leader = (r == 0);
+    const bool ep_leader = (r == 0);
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     uint32_t tc = 0, sl = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+    for (int t = pair; t < ntiles; t += npairs, ++tc) {
       const TileInfo ti = decode_tile(p, t);
       const uint32_t ab = tc & 1u;
+      const int row = ti.mb * 256 + static_cast<int>(rank) * 128;
       if (!warp_wait(&acc_full[ab], (tc >> 1) & 1u, abort_flag, kErrGemm | 4)) goto done;
       tc_fence_after();
       const uint32_t acol = trow + ab * 256;
@@ -211,46 +225,74 @@ __global__ void __launch_bounds__(256, 1)
           tmem_wait_ld();
         }
         uint8_t* stg = smem + Cfg::SMEM_STG + (sl & 1u) * Cfg::STG_BYTES;
-        if (leader) tma_store_wait_read<1>();  // the store issued from this slab two steps ago has read it
+        if (ep_leader) tma_store_wait_read<1>();  // the store issued from this slab two steps ago has read it
         named_bar_sync(1, 128);
         stage_row(stg, r, v);
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
-        if (leader) {
+        if (ep_leader) {
           if (ti.dw)
-            tma_store_2d(&tm_gw, stg, ti.nb * 256 + s * (f16out ? 64 : 32), p.v_begin + ti.mb * 128);
+            tma_store_2d(&tm_gw, stg, ti.nb * 256 + s * (f16out ? 64 : 32), p.v_begin + row);
           else
-            tma_reduce_add_2d(&tm_dh, stg, ti.nb * 256 + s * 32, ti.mb * 128);
+            tma_reduce_add_2d(&tm_dh, stg, ti.nb * 256 + s * 32, row);
           tma_store_commit();
         }
       }
+      // every thread of this CTA has read its accumulator rows: release them to the leader
       tc_fence_before();
-      mbar_arrive(&acc_empty[ab]);
+      named_bar_sync(1, 128);
+      if (ep_leader) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[ab]), 0));
     }
-    if (leader) tma_store_wait_all<0>();
+    if (ep_leader) tma_store_wait_all<0>();
   }
 done:
   tc_fence_before();
   __syncthreads();
-  if (*abort_flag) drain_after_abort(warp == 1 && lane == 0, spare);
+  if (*abort_flag) drain_after_abort_pair(warp == 1 && lane == 0 && leader, spare);
+  cluster_sync_all();  // neither CTA releases TMEM / shared memory while its peer may use them
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
 template <bool kBF16, int NS>
-static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int grid, cudaStream_t st) {
+static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pairs, cudaStream_t st) {
   using Cfg = GemmCfg<NS>;
   auto kern = gemm_kernel<kBF16, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
-  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(m.ds_k, m.ds_mn, m.h_mn, m.w_mn, m.gw, m.dh, prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+  cfg.stream = st;
+  cfg.gridDim = dim3(2 * 74, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess) return e;
+  const int tiles = prm.dw_tiles + prm.dh_tiles;
+  int pairs = std::min(std::min(clusters, max_pairs), tiles);
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  static bool reported = false;
+  if (!reported && getenv("SWVR_DEBUG")) {
+    fprintf(stderr, "[swvr] gemm_kernel: %d co-resident 2-CTA clusters, launching %d pairs for %d tiles\n", clusters,
+            pairs, tiles);
+    reported = true;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, m.ds_k, m.ds_mn, m.h_mn, m.w_mn, m.gw, m.dh, prm);
 }
 
-cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int grid, cudaStream_t st) {
-  return bf16 ? launch<true, 4>(maps, prm, grid, st) : launch<false, 4>(maps, prm, grid, st);
+cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs,
+                               cudaStream_t st) {
+  return bf16 ? launch<true, 6>(maps, prm, max_pairs, st) : launch<false, 6>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc
