@@ -290,9 +290,9 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   b.max_units = 1;
   for (int64_t rows : {C, p.vocab % C}) {
     if (rows <= 0) continue;
-    const int VTc = static_cast<int>(ceil_div(rows, 128));
+    const int VTc = static_cast<int>(ceil_div(rows, 256));
     int TS, per_t;
-    choose_ts(VTc, b.NT, b.sms, &TS, &per_t);
+    choose_ts(VTc, b.NT, b.sms / 2, &TS, &per_t);
     b.max_units = std::max(b.max_units, VTc * TS);
   }
   size_t off = 0;
@@ -305,9 +305,9 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   b.off_dh = off;
   if (b.need_h && !g.grad_h_acc) off += align_up(static_cast<size_t>(p.n_tokens) * p.hidden * 4, 256);
   b.off_de = off;
-  if (b.need_E) off += align_up(static_cast<size_t>(b.max_units) * 128 * p.embed_dim * 4, 256);
+  if (b.need_E) off += align_up(static_cast<size_t>(b.max_units) * 256 * p.embed_dim * 4, 256);
   b.off_db = off;
-  if (b.need_b) off += align_up(static_cast<size_t>(b.max_units) * 128 * 4, 256);
+  if (b.need_b) off += align_up(static_cast<size_t>(b.max_units) * 256 * 4, 256);
   b.bytes = off + 256;
   return b;
 }
@@ -347,9 +347,10 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
 
   tc::BwdScoresMaps sm;
   SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));
-  SWVR_TRY(make_map(&sm.h, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.h64, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
   SWVR_TRY(make_map(&sm.e, p.E, p.compute_dtype, D, V, p.lde * 2, 64, 128));
-  SWVR_TRY(make_map(&sm.go, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.go64, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 64));
+  SWVR_TRY(make_map(&sm.go128, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 128));
   tc::GemmMaps gm;
   if (b.need_ds) {
     SWVR_TRY(make_map(&gm.h_mn, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
@@ -371,9 +372,9 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
   for (int64_t v0 = 0; v0 < V; v0 += b.C) {
     const int64_t v1 = std::min<int64_t>(v0 + b.C, V);
     const int rows = static_cast<int>(v1 - v0);
-    const int VTc = static_cast<int>(ceil_div(rows, 128));
+    const int VTc = static_cast<int>(ceil_div(rows, 256));
     int TS, per_t;
-    choose_ts(VTc, b.NT, b.sms, &TS, &per_t);
+    choose_ts(VTc, b.NT, b.sms / 2, &TS, &per_t);
     tc::BwdScoresParams sp{};
     sp.N = static_cast<int>(N);
     sp.K = static_cast<int>(K);
@@ -400,16 +401,16 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
       SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
       sm.ds = gm.ds_k;
     } else {
-      sm.ds = sm.go;  // unused
+      sm.ds = sm.go128;  // unused
     }
     {
       ProfScope ps(kProfBwdScores, st);
-      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, std::min(sp.units, b.sms), st));
+      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, b.sms / 2, st));
     }
     if (part_de || part_db) {
       void* gE = g.grad_E;
       ProfScope ps(kProfReduce, st);
-      SWVR_CUDA(small::reduce_de_db(part_de, part_db, TS, per_t, b.NT, static_cast<int>(v0), rows, D, gE,
+      SWVR_CUDA(small::reduce_de_db(part_de, part_db, TS, per_t, b.NT, static_cast<int>(v0), rows, 256, D, gE,
                                     g.grad_E_dtype, g.ld_grad_E, g.grad_bias, g.grad_bias_dtype, st));
     }
     if (b.need_ds) {

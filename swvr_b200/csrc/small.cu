@@ -61,19 +61,20 @@ cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, con
 }
 
 // ------------------------------------------------------------------ dE / db reduction
-// Row v of the chunk: sum its TS token-split partial slots in split order.
+// Row v of the chunk: sum its TS token-split partial slots in split order.  Slots are
+// grouped per vocabulary tile of `tile_rows` rows: slot((vt*TS + ts)*tile_rows + r).
 __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const float* __restrict__ part_db, int TS,
-                                    int per_t, int NT, int v_begin, int64_t D, void* gE, int gE_dt, int64_t ld_gE,
-                                    void* gb, int gb_dt) {
+                                    int per_t, int NT, int v_begin, int tile_rows, int64_t D, void* gE, int gE_dt,
+                                    int64_t ld_gE, void* gb, int gb_dt) {
   const int rr = blockIdx.x;  // row within the chunk
-  const int vt = rr / 128, r = rr % 128;
+  const int vt = rr / tile_rows, r = rr % tile_rows;
   const int64_t v = v_begin + rr;
   if (part_de) {
     for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
       float s = 0.f;
       for (int ts = 0; ts < TS; ++ts) {
         if (ts * per_t >= NT) break;
-        s += part_de[((static_cast<int64_t>(vt) * TS + ts) * 128 + r) * D + d];
+        s += part_de[((static_cast<int64_t>(vt) * TS + ts) * tile_rows + r) * D + d];
       }
       store_f(gE, gE_dt, v * ld_gE + d, s);
     }
@@ -82,17 +83,18 @@ __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const flo
     float s = 0.f;
     for (int ts = 0; ts < TS; ++ts) {
       if (ts * per_t >= NT) break;
-      s += part_db[(static_cast<int64_t>(vt) * TS + ts) * 128 + r];
+      s += part_db[(static_cast<int64_t>(vt) * TS + ts) * tile_rows + r];
     }
     store_f(gb, gb_dt, v, s);
   }
 }
 
 cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
-                         int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt, cudaStream_t st) {
+                         int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt,
+                         cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  reduce_de_db_kernel<<<rows, D >= 128 ? 128 : 64, 0, st>>>(part_de, part_db, TS, per_t, NT, v_begin, D, gE, gE_dt,
-                                                             ld_gE, gb, gb_dt);
+  reduce_de_db_kernel<<<rows, D >= 128 ? 128 : 64, 0, st>>>(part_de, part_db, TS, per_t, NT, v_begin, tile_rows, D, gE,
+                                                             gE_dt, ld_gE, gb, gb_dt);
   return cudaGetLastError();
 }
 

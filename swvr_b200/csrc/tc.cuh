@@ -37,20 +37,26 @@ struct BwdScoresParams {
   int bias_dt;
   const float* lse;    // [N]
   const float* delta;  // [N]
-  int NT, VT;          // 128-token tiles, 128-row vocabulary tiles of the chunk
+  int NT, VT;          // 128-token tiles, 256-row vocabulary pair tiles of the chunk
   int TS, per_t, units;  // token splits, token tiles per split, VT * TS
   void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null
   int64_t ld_ds;
-  float* part_de;      // [units * 128 * D] or null
-  float* part_db;      // [units * 128] or null
+  float* part_de;      // [units * 256 * D] or null
+  float* part_db;      // [units * 256] or null
 };
 
 struct BwdScoresMaps {
-  CUtensorMap w, h, e, go, ds;  // ds: this chunk's dS^T [rows, Npad], box {64, 128} (TMA store)
+  CUtensorMap w;      // W, box {64, 128}
+  CUtensorMap h64;    // h, box {64, 64} (half a token tile)
+  CUtensorMap e;      // E, box {64, 128}
+  CUtensorMap go64;   // gO in the compute dtype [N, DP], box {64, 64}
+  CUtensorMap go128;  // the same, box {64, 128}
+  CUtensorMap ds;     // this chunk's dS^T [rows, Npad], box {64, 128} (TMA store)
 };
 
+// Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                     int grid, cudaStream_t st);
+                                     int max_pairs, cudaStream_t st);
 
 // ------------------------------------------------------------------ backward: dW / dh GEMMs
 struct GemmParams {

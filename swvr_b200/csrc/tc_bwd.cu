@@ -1,13 +1,19 @@
-// Tensor-core (tcgen05) backward score kernel on sm_100a, vocabulary-major.
+// Tensor-core (tcgen05) backward score kernel on sm_100a, vocabulary-major, 2-SM.
 //
-// A CTA owns a 128-row vocabulary tile of the current chunk (the MMA M dimension, one
-// TMEM lane and one thread per vocabulary row) and walks a range of 128-token tiles:
+// A CTA pair (cluster of 2) owns a 256-row vocabulary tile of the current chunk (the MMA M
+// dimension: 128 rows, TMEM lanes and threads per CTA) and walks a range of 128-token tiles:
 //   S^T  = W_tile . h_tile^T                 (K = hidden; recompute of the forward scores)
 //   dP^T = E_tile . dO_tile^T                (K = D)
 //   P    = 2^(S*s*log2e + b*log2e - LSE*log2e),   dS = P * (dP - delta)
 //   db  += rowsum(dS)                        (thread-local: the thread owns the row)
-//   dE  += P^T . dO_tile                     (tcgen05.mma, A = P read from TMEM, D in TMEM)
+//   dE  += P^T . dO_tile                     (A = P read from TMEM, D in TMEM)
 //   dS^T * s is stored in the compute dtype for the dh / dW GEMMs (tc_gemm.cu).
+// All three products are tcgen05.mma.cta_group::2 issued by the even CTA: each CTA stages
+// its own 128 W rows and half of the h tile (64 tokens), so a pair moves 24 KB per CTA per
+// K-block for 2*256*128*64 FLOP (87 FLOP/B, against 64 for a single-CTA 128x128 tile).
+// gO is staged twice per token tile: the CTA's 64-token half, K-major, as the B operand of
+// dP^T, and the CTA's 64-column half of all 128 tokens, MN-major, as the B operand of dE
+// (whose N is padded to 128, so for D <= 64 the odd CTA's half is zero fill).
 // dE and db of a unit go to a partial slot; reduce_de_db_kernel (small.cu) sums the token
 // splits of a vocabulary row in a fixed order, so the result is deterministic.
 //
@@ -19,48 +25,56 @@
 namespace swvr {
 namespace tc {
 
-template <bool kBF16, int DP, int NS>
+// KH: 64-wide K halves per pipeline stage (2 -> 8 MMAs per barrier round trip of the
+// single MMA-issuing thread); STG: dS^T goes out through a staged TMA store (else direct
+// 16-byte stores from registers, which frees the staging tile for a deeper pipeline).
+template <bool kBF16, int DP, int NS, int KH, bool STG>
 struct BwdCfg {
-  static constexpr int BOX = 128 * 128;  // 128 rows x 128 bytes (64 16-bit elements)
-  static constexpr int A_BYTES = BOX, B_BYTES = BOX;
-  static constexpr int E_BYTES = (DP / 64) * BOX;
-  static constexpr int GO_BYTES = (DP / 64) * BOX;
+  static constexpr int BOX = 128 * 128;   // 128 rows x 128 bytes (64 16-bit elements)
+  static constexpr int HBOX = 64 * 128;   // 64 rows x 128 bytes
+  static constexpr int A_BYTES = KH * BOX;   // this CTA's 128 W rows x 64*KH K
+  static constexpr int B_BYTES = KH * HBOX;  // this CTA's 64 h rows x 64*KH K
+  static constexpr int E_BYTES = (DP / 64) * BOX;     // this CTA's 128 E rows x DP
+  static constexpr int GOK_BYTES = (DP / 64) * HBOX;  // this CTA's 64 tokens x DP (K-major)
+  static constexpr int GOM_BYTES = BOX;               // 128 tokens x this CTA's 64 columns (MN-major)
   static constexpr int SMEM_A = 0;
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
   static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
-  static constexpr int SMEM_GO = SMEM_E + E_BYTES;
-  static constexpr int SMEM_STG = SMEM_GO + 2 * GO_BYTES;  // dS tile staging: two 128 x 64 boxes
-  static constexpr int SMEM_LSE = SMEM_STG + 2 * BOX;
+  static constexpr int SMEM_GOK = SMEM_E + E_BYTES;
+  static constexpr int SMEM_GOM = SMEM_GOK + 2 * GOK_BYTES;
+  static constexpr int SMEM_STG = SMEM_GOM + 2 * GOM_BYTES;  // dS tile staging: two 128 x 64 boxes
+  static constexpr int SMEM_LSE = SMEM_STG + (STG ? 2 * BOX : 0);
   static constexpr int SMEM_DELTA = SMEM_LSE + 512;
   static constexpr int SMEM_BAR = SMEM_DELTA + 512;
   static constexpr int NBAR = 2 * NS + 13;
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
-  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;
-  static_assert(DE_COL + DP <= 512, "TMEM budget");
+  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;  // dE: 128 columns (N padded)
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+  static_assert(DP == 64 || DP == 128, "D padding");
 };
 
-template <bool kBF16, int DP, int NS>
+template <bool kBF16, int DP, int NS, int KH, bool STG>
 __global__ void __launch_bounds__(256, 1)
-    bwd_scores_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_h,
-                      const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_go,
-                      const __grid_constant__ CUtensorMap tm_ds, const BwdScoresParams p) {
-  using Cfg = BwdCfg<kBF16, DP, NS>;
+    bwd_scores_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_h64,
+                      const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_go64,
+                      const __grid_constant__ CUtensorMap tm_go128, const __grid_constant__ CUtensorMap tm_ds,
+                      const BwdScoresParams p) {
+  using Cfg = BwdCfg<kBF16, DP, NS, KH, STG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + NS;
-  uint64_t* e_full = bars + 2 * NS;
-  uint64_t* e_empty = e_full + 1;
-  uint64_t* go_full = e_empty + 1;    // [2]
-  uint64_t* go_empty = go_full + 2;   // [2]
-  uint64_t* s_full = go_empty + 2;    // [2]
-  uint64_t* dp_full = s_full + 2;
-  uint64_t* p_ready = dp_full + 1;    // [2]
-  uint64_t* de_full = p_ready + 2;
-  uint64_t* de_free = de_full + 1;
+  uint64_t* full = bars;              // [NS] leader: both CTAs' bytes
+  uint64_t* empty = bars + NS;        // [NS] both (multicast commit)
+  uint64_t* e_full = bars + 2 * NS;   // leader: both CTAs' bytes
+  uint64_t* e_empty = e_full + 1;     // both
+  uint64_t* go_full = e_empty + 1;    // [2] leader: both CTAs' bytes
+  uint64_t* go_empty = go_full + 2;   // [2] both
+  uint64_t* s_full = go_empty + 2;    // [2] both
+  uint64_t* dp_full = s_full + 2;     // both
+  uint64_t* p_ready = dp_full + 1;    // [2] leader: one arrival per CTA
+  uint64_t* de_full = p_ready + 2;    // both
+  uint64_t* de_free = de_full + 1;    // leader: one arrival per CTA
   uint64_t* spare = de_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -69,6 +83,9 @@ __global__ void __launch_bounds__(256, 1)
 
   const bool need_ds = p.ds != nullptr, need_de = p.part_de != nullptr, need_db = p.part_db != nullptr;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
@@ -80,51 +97,62 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&go_full[b], 1);
       mbar_init(&go_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_ready[b], 128);
+      mbar_init(&p_ready[b], 2);
     }
     mbar_init(dp_full, 1);
     mbar_init(de_full, 1);
-    mbar_init(de_free, 128);
+    mbar_init(de_free, 2);
     mbar_init(spare, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
-    tma_prefetch_desc(&tm_h);
+    tma_prefetch_desc(&tm_h64);
     tma_prefetch_desc(&tm_e);
-    tma_prefetch_desc(&tm_go);
+    tma_prefetch_desc(&tm_go64);
+    tma_prefetch_desc(&tm_go128);
     if (p.ds) tma_prefetch_desc(&tm_ds);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_holder, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int KB = (p.K + 63) / 64;
+  const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
+      // ------------------------------------------------------------ TMA producer (both CTAs)
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      for (int u = pair; u < p.units; u += npairs) {
         const int vt = u / p.TS, ts = u % p.TS;
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         if (it1 <= it0) continue;
-        const int vrow0 = p.v_begin + vt * 128;
+        const int vrow0 = p.v_begin + vt * 256 + static_cast<int>(rank) * 128;
         if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
-        mbar_arrive_expect_tx(e_full, Cfg::E_BYTES);
+        if (leader) mbar_arrive_expect_tx(e_full, 2 * Cfg::E_BYTES);
+        {
+          const uint32_t eb = mapa_shared(smem_u32(e_full), 0);
 #pragma unroll
-        for (int c = 0; c < DP / 64; ++c) tma_load_2d(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, e_full, c * 64, vrow0);
+          for (int c = 0; c < DP / 64; ++c) tma_load_2d_pair(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, eb, c * 64, vrow0);
+        }
         for (int it = it0; it < it1; ++it, ++g) {
+          const int trow = it * 128 + static_cast<int>(rank) * 64;
           for (int kb = 0; kb < KB; ++kb) {
             if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrBwdScores | 2)) goto done;
-            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
-            tma_load_2d(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES, &tm_w, &full[stage], kb * 64, vrow0);
-            tma_load_2d(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES, &tm_h, &full[stage], kb * 64, it * 128);
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+#pragma unroll
+            for (int hk = 0; hk < KH; ++hk) {
+              const int k0 = (kb * KH + hk) * 64;  // past K the boxes read zero fill
+              tma_load_2d_pair(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES + hk * Cfg::BOX, &tm_w, fb, k0, vrow0);
+              tma_load_2d_pair(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES + hk * Cfg::HBOX, &tm_h64, fb, k0, trow);
+            }
             if (++stage == NS) {
               stage = 0;
               sphase ^= 1u;
@@ -132,23 +160,28 @@ __global__ void __launch_bounds__(256, 1)
           }
           const uint32_t gb = g & 1u, use = g >> 1;
           if (!mbar_wait(&go_empty[gb], (use & 1u) ^ 1u, abort_flag, kErrBwdScores | 3)) goto done;
-          mbar_arrive_expect_tx(&go_full[gb], Cfg::GO_BYTES);
+          if (leader) mbar_arrive_expect_tx(&go_full[gb], 2 * (Cfg::GOK_BYTES + Cfg::GOM_BYTES));
+          const uint32_t gob = mapa_shared(smem_u32(&go_full[gb]), 0);
 #pragma unroll
           for (int c = 0; c < DP / 64; ++c)
-            tma_load_2d(smem + Cfg::SMEM_GO + gb * Cfg::GO_BYTES + c * Cfg::BOX, &tm_go, &go_full[gb], c * 64,
-                        it * 128);
+            tma_load_2d_pair(smem + Cfg::SMEM_GOK + gb * Cfg::GOK_BYTES + c * Cfg::HBOX, &tm_go64, gob, c * 64, trow);
+          tma_load_2d_pair(smem + Cfg::SMEM_GOM + gb * Cfg::GOM_BYTES, &tm_go128, gob, static_cast<int>(rank) * 64,
+                           it * 128);
         }
         ++uc;
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      const uint32_t idS = idesc_f16(kBF16, 128, 128, false, false);
-      const uint32_t idDE = idesc_f16(kBF16, 128, DP, false, true);
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      const uint32_t idS = idesc_f16(kBF16, 256, 128, false, false);
+      const uint32_t idDE = idesc_f16(kBF16, 256, 128, false, true);
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
       const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E);
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      // stage-0 descriptors; a stage / K half / 16-wide K step adds (byte offset >> 4)
+      const uint64_t da0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);
+      const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
+      for (int u = pair; u < p.units; u += npairs) {
         const int ts = u % p.TS;
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         const int n = it1 - it0;
@@ -160,32 +193,31 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t b = g & 1u;
             for (int kb = 0; kb < KB; ++kb) {
               if (!mbar_wait(&full[stage], sphase, abort_flag, kErrBwdScores | 5)) goto done;
-              tc_fence_after();
-              const uint32_t abase = smem_u32(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES);
-              const uint32_t bbase = smem_u32(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES);
+              const uint64_t sa = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));
+              const uint64_t sb = static_cast<uint64_t>(stage * (Cfg::B_BYTES >> 4));
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks)
-                umma_ss(tmem + Cfg::S_COL + b * 128, sdesc_sw128(abase + ks * 32, 16, 1024),
-                        sdesc_sw128(bbase + ks * 32, 16, 1024), idS, (kb | ks) ? 1u : 0u);
-              umma_commit(&empty[stage]);
+              for (int k8 = 0; k8 < 4 * KH; ++k8)
+                umma2_ss(tmem + Cfg::S_COL + b * 128, da0 + sa + (k8 >> 2) * (Cfg::BOX >> 4) + (k8 & 3) * 2,
+                         db0 + sb + (k8 >> 2) * (Cfg::HBOX >> 4) + (k8 & 3) * 2, idS, (kb | k8) ? 1u : 0u);
+              umma2_commit_mc(&empty[stage], 3);
               if (++stage == NS) {
                 stage = 0;
                 sphase ^= 1u;
               }
             }
-            umma_commit(&s_full[b]);
-            // dP^T = E . dO^T into the single dP buffer: the previous tile's gradient pass
-            // must have finished reading it.
+            umma2_commit_mc(&s_full[b], 3);
+            // dP^T = E . dO^T into the single dP buffer: both CTAs' gradient passes of the
+            // previous tile must have finished reading it.
             if (j > 0 && !mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 6))
               goto done;
             if (!mbar_wait(&go_full[b], (g >> 1) & 1u, abort_flag, kErrBwdScores | 7)) goto done;
             tc_fence_after();
-            const uint32_t gobase = smem_u32(smem + Cfg::SMEM_GO + b * Cfg::GO_BYTES);
+            const uint32_t gokbase = smem_u32(smem + Cfg::SMEM_GOK + b * Cfg::GOK_BYTES);
 #pragma unroll
             for (int ks = 0; ks < DP / 16; ++ks)
-              umma_ss(tmem + Cfg::DP_COL, sdesc_sw128(ebase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024),
-                      sdesc_sw128(gobase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024), idS, ks ? 1u : 0u);
-            umma_commit(dp_full);
+              umma2_ss(tmem + Cfg::DP_COL, sdesc_sw128(ebase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024),
+                       sdesc_sw128(gokbase + (ks >> 2) * Cfg::HBOX + (ks & 3) * 32, 16, 1024), idS, ks ? 1u : 0u);
+            umma2_commit_mc(dp_full, 3);
             ++g;
           }
           if (j > 0) {
@@ -196,22 +228,22 @@ __global__ void __launch_bounds__(256, 1)
               const bool first = (j == 1);
               if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
               tc_fence_after();
-              const uint32_t gobase = smem_u32(smem + Cfg::SMEM_GO + bb * Cfg::GO_BYTES);
+              const uint32_t gombase = smem_u32(smem + Cfg::SMEM_GOM + bb * Cfg::GOM_BYTES);
 #pragma unroll
               for (int ks = 0; ks < 8; ++ks)
-                umma_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + bb * 128 + ks * 8,
-                        sdesc_sw128(gobase + ks * 2048, Cfg::BOX, 1024), idDE, (first && ks == 0) ? 0u : 1u);
+                umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + bb * 128 + ks * 8,
+                         sdesc_sw128(gombase + ks * 2048, Cfg::BOX, 1024), idDE, (first && ks == 0) ? 0u : 1u);
             }
-            umma_commit(&go_empty[bb]);
+            umma2_commit_mc(&go_empty[bb], 3);
           }
         }
-        umma_commit(e_empty);
-        if (need_de) umma_commit(de_full);
+        umma2_commit_mc(e_empty, 3);
+        if (need_de) umma2_commit_mc(de_full, 3);
         ++uc;
       }
     }
   } else if (warp >= 4) {
-    // -------------------------------------------------------------- gradient warps
+    // -------------------------------------------------------------- gradient warps (both CTAs)
     // lse_s holds -LSE*log2e and delta_s holds -delta for the current token tile, so each
     // pair of tokens costs a handful of packed f32x2 ops.  dS*s goes to a 128B-swizzled
     // staging tile that one thread stores with two TMA bulk copies per token tile.
@@ -219,12 +251,15 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     uint8_t* stg = smem + Cfg::SMEM_STG;
     const float2 sc2v = make_float2(p.sc2, p.sc2), scalev = make_float2(p.scale, p.scale);
+    const uint32_t p_ready_leader = mapa_shared(smem_u32(p_ready), 0);
+    const uint32_t de_free_leader = mapa_shared(smem_u32(de_free), 0);
     uint32_t g = 0, uc = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    for (int u = pair; u < p.units; u += npairs) {
       const int vt = u / p.TS, ts = u % p.TS;
       const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
       if (it1 <= it0) continue;
-      const int vrow = p.v_begin + vt * 128 + r;
+      const int local_row0 = vt * 256 + static_cast<int>(rank) * 128;  // within the chunk
+      const int vrow = p.v_begin + local_row0 + r;
       const bool vvalid = vrow < p.v_end;
       const float b2 = (p.bias != nullptr && vvalid) ? load_f(p.bias, p.bias_dt, vrow) * kLog2e : 0.f;
       const float2 b2v = make_float2(b2, b2);
@@ -232,7 +267,7 @@ __global__ void __launch_bounds__(256, 1)
       for (int it = it0; it < it1; ++it, ++g) {
         const int t0 = it * 128;
         // the previous tile's dS store must have finished reading the staging tile
-        if (need_ds && r == 0) tma_store_wait_read<0>();
+        if (STG && need_ds && r == 0) tma_store_wait_read<0>();
         named_bar_sync(1, 128);
         {
           const int t = t0 + r;
@@ -272,33 +307,38 @@ __global__ void __launch_bounds__(256, 1)
               pk_p[i / 2] = pack2<kBF16>(pv.x, pv.y);
             }
           }
-          if (need_ds) {
+          if (STG && need_ds) {
             // tokens [32c, 32c + 32) of row r: box c/2, 16-byte chunks (c%2)*4 + q, 128B swizzle
             uint8_t* row = stg + (c >> 1) * Cfg::BOX + r * 128;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const int j = (c & 1) * 4 + q;
-              *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) =
+              const int jj = (c & 1) * 4 + q;
+              *reinterpret_cast<uint4*>(row + ((jj ^ (r & 7)) << 4)) =
                   make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
             }
+          } else if (need_ds && vvalid) {
+            // 64 contiguous bytes of row r: tokens [t0 + 32c, t0 + 32c + 32)
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.ds) +
+                                                  static_cast<int64_t>(local_row0 + r) * p.ld_ds + t0 + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
           }
           if (need_de) tmem_st16(sbase + c * 16, pk_p);
         }
-        if (need_ds) {
-          fence_proxy_async_smem();
-          named_bar_sync(1, 128);
-          if (r == 0) {
-            const int row0 = vt * 128;
-            tma_store_2d(&tm_ds, stg, t0, row0);
-            tma_store_2d(&tm_ds, stg + Cfg::BOX, t0 + 64, row0);
+        if (need_de) tmem_wait_st();
+        if (STG && need_ds) fence_proxy_async_smem();
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (r == 0) {
+          if (STG && need_ds) {
+            tma_store_2d(&tm_ds, stg, t0, local_row0);
+            tma_store_2d(&tm_ds, stg + Cfg::BOX, t0 + 64, local_row0);
             tma_store_commit();
           }
+          mbar_arrive_cluster(p_ready_leader + b * 8);
         }
-        if (need_de) tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_ready[b]);
       }
-      const int64_t slot = static_cast<int64_t>(u) * 128 + r;
+      const int64_t slot = static_cast<int64_t>(u) * 256 + static_cast<int>(rank) * 128 + r;
       if (need_de) {
         if (!warp_wait(de_full, uc & 1u, abort_flag, kErrBwdScores | 12)) goto done;
         tc_fence_after();
@@ -316,37 +356,59 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(de_free);
+        named_bar_sync(1, 128);
+        if (r == 0) mbar_arrive_cluster(de_free_leader);
       }
       if (need_db && vvalid) p.part_db[slot] = db.x + db.y;
       ++uc;
     }
-    if (need_ds && r == 0) tma_store_wait_all<0>();
+    if (STG && need_ds && r == 0) tma_store_wait_all<0>();
   }
 done:
   tc_fence_before();
   __syncthreads();
-  if (*abort_flag) drain_after_abort(warp == 1 && lane == 0, spare);
+  if (*abort_flag) drain_after_abort_pair(warp == 1 && lane == 0 && leader, spare);
+  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
-template <bool kBF16, int DP, int NS>
-static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int grid, cudaStream_t st) {
-  using Cfg = BwdCfg<kBF16, DP, NS>;
-  auto kern = bwd_scores_kernel<kBF16, DP, NS>;
+template <bool kBF16, int DP, int NS, int KH, bool STG>
+static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int max_pairs, cudaStream_t st) {
+  using Cfg = BwdCfg<kBF16, DP, NS, KH, STG>;
+  auto kern = bwd_scores_kernel<kBF16, DP, NS, KH, STG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
-  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(m.w, m.h, m.e, m.go, m.ds, prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+  cfg.stream = st;
+  cfg.gridDim = dim3(2 * 74, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess) return e;
+  int pairs = std::min(std::min(clusters, max_pairs), prm.units);
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  return cudaLaunchKernelEx(&cfg, kern, m.w, m.h64, m.e, m.go64, m.go128, m.ds, prm);
 }
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                     int grid, cudaStream_t st) {
-  if (DP == 64) return bf16 ? launch_bwd<true, 64, 4>(maps, prm, grid, st) : launch_bwd<false, 64, 4>(maps, prm, grid, st);
-  return bf16 ? launch_bwd<true, 128, 3>(maps, prm, grid, st) : launch_bwd<false, 128, 3>(maps, prm, grid, st);
+                                     int max_pairs, cudaStream_t st) {
+  if (DP == 64)
+    return bf16 ? launch_bwd<true, 64, 3, 2, false>(maps, prm, max_pairs, st)
+                : launch_bwd<false, 64, 3, 2, false>(maps, prm, max_pairs, st);
+  return bf16 ? launch_bwd<true, 128, 4, 1, true>(maps, prm, max_pairs, st)
+              : launch_bwd<false, 128, 4, 1, true>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc

@@ -5,8 +5,10 @@
 //
 // 2-SM design: CTA pairs (clusters of 2) compute 256 x 256 output tiles with
 // tcgen05.mma.cta_group::2.  Each CTA of a pair stages its own 128 rows of A and its own
-// 128-column half of B per K-block (32 KB instead of 48 KB for a single-CTA 128 x 256
-// tile), so shared-memory traffic per FLOP drops by a third.  The even CTA (the leader)
+// 128-column half of B (128 FLOP per staged byte, against 85 for a single-CTA 128 x 256
+// tile).  K-blocks are 128 wide (8 MMAs per pipeline stage): the single MMA-issuing
+// thread pays its barrier wait and loop overhead once per 8 MMAs, which the shallow MMA
+// issue queue would otherwise expose as tensor-pipe bubbles.  The even CTA (the leader)
 // issues every MMA; its commits arrive on the barriers of both CTAs, and both CTAs' TMA
 // loads count their bytes on the leader's barrier.  Each CTA's epilogue reads its own 128
 // rows from its TMEM and writes them with TMA: a store for dW (cast to the W dtype) and an
@@ -27,8 +29,9 @@ namespace tc {
 
 template <int NS>
 struct GemmCfg {
-  static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 64 16-bit elements
-  static constexpr int B_BYTES = 128 * 128;  // this CTA's 128 columns: two 64 x 64 boxes
+  static constexpr int HALF = 128 * 128;     // one 64-wide K half: 128 rows (A) or columns (B)
+  static constexpr int A_BYTES = 2 * HALF;   // this CTA's 128 rows x 128 16-bit elements
+  static constexpr int B_BYTES = 2 * HALF;   // this CTA's 128 columns x 128 K
   static constexpr int BOX64 = 64 * 128;     // one 64 x 64 box
   static constexpr int STG_BYTES = 128 * 128;
   static constexpr int SMEM_A = 0;
@@ -53,13 +56,13 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
     ti.dw = true;
     ti.mb = t / p.dw_nt;
     ti.nb = t % p.dw_nt;
-    ti.kblocks = p.dw_kb;
+    ti.kblocks = (p.dw_kb + 1) / 2;  // 128-wide K-blocks
   } else {
     t -= p.dw_tiles;
     ti.dw = false;
     ti.mb = t / p.dh_nt;
     ti.nb = t % p.dh_nt;
-    ti.kblocks = p.dh_kb;
+    ti.kblocks = (p.dh_kb + 1) / 2;
   }
   return ti;
 }
@@ -139,17 +142,21 @@ __global__ void __launch_bounds__(256, 1)
           if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrGemm | 1)) goto done;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-          uint8_t* a = smem + Cfg::SMEM_A + stage * Cfg::A_BYTES;
-          uint8_t* b = smem + Cfg::SMEM_B + stage * Cfg::B_BYTES;
-          if (ti.dw) {
-            tma_load_2d_pair(a, &tm_ds_k, fb, kb * 64, row);
-            tma_load_2d_pair(b, &tm_h_mn, fb, col, kb * 64);
-            tma_load_2d_pair(b + Cfg::BOX64, &tm_h_mn, fb, col + 64, kb * 64);
-          } else {
-            tma_load_2d_pair(a, &tm_ds_mn, fb, row, kb * 64);
-            tma_load_2d_pair(a + Cfg::BOX64, &tm_ds_mn, fb, row + 64, kb * 64);
-            tma_load_2d_pair(b, &tm_w_mn, fb, col, p.v_begin + kb * 64);
-            tma_load_2d_pair(b + Cfg::BOX64, &tm_w_mn, fb, col + 64, p.v_begin + kb * 64);
+#pragma unroll
+          for (int hk = 0; hk < 2; ++hk) {
+            const int k0 = (2 * kb + hk) * 64;  // past K the boxes read zero fill
+            uint8_t* a = smem + Cfg::SMEM_A + stage * Cfg::A_BYTES + hk * Cfg::HALF;
+            uint8_t* b = smem + Cfg::SMEM_B + stage * Cfg::B_BYTES + hk * Cfg::HALF;
+            if (ti.dw) {
+              tma_load_2d_pair(a, &tm_ds_k, fb, k0, row);
+              tma_load_2d_pair(b, &tm_h_mn, fb, col, k0);
+              tma_load_2d_pair(b + Cfg::BOX64, &tm_h_mn, fb, col + 64, k0);
+            } else {
+              tma_load_2d_pair(a, &tm_ds_mn, fb, row, k0);
+              tma_load_2d_pair(a + Cfg::BOX64, &tm_ds_mn, fb, row + 64, k0);
+              tma_load_2d_pair(b, &tm_w_mn, fb, col, p.v_begin + k0);
+              tma_load_2d_pair(b + Cfg::BOX64, &tm_w_mn, fb, col + 64, p.v_begin + k0);
+            }
           }
           if (++stage == NS) {
             stage = 0;
@@ -163,6 +170,10 @@ __global__ void __launch_bounds__(256, 1)
       // ------------------------------------------------------------ MMA issuer (leader only)
       const uint32_t id_dw = idesc_f16(kBF16, 256, 256, false, true);
       const uint32_t id_dh = idesc_f16(kBF16, 256, 256, true, true);
+      // descriptors of stage 0; a stage / K-half / 16-wide K step adds a byte offset >> 4
+      const uint64_t da_k = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);           // K-major A (dW)
+      const uint64_t da_mn = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), Cfg::BOX64, 1024);  // MN-major A (dh)
+      const uint64_t db_mn = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), Cfg::BOX64, 1024);  // MN-major B
       uint32_t stage = 0, sphase = 0, tc = 0;
       for (int t = pair; t < ntiles; t += npairs, ++tc) {
         const TileInfo ti = decode_tile(p, t);
@@ -170,18 +181,17 @@ __global__ void __launch_bounds__(256, 1)
         if (!mbar_wait(&acc_empty[ab], ((tc >> 1) & 1u) ^ 1u, abort_flag, kErrGemm | 2)) goto done;
         tc_fence_after();
         const uint32_t dcol = tmem + ab * 256;
+        const uint64_t da = ti.dw ? da_k : da_mn;
+        const uint32_t id = ti.dw ? id_dw : id_dh;
+        const uint32_t a_step = ti.dw ? (32u >> 4) : (2048u >> 4);  // one 16-wide K step of A
         for (int kb = 0; kb < ti.kblocks; ++kb) {
           if (!mbar_wait(&full[stage], sphase, abort_flag, kErrGemm | 3)) goto done;
-          tc_fence_after();
-          const uint32_t abase = smem_u32(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES);
-          const uint32_t bbase = smem_u32(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES);
+          const uint64_t so = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));  // A and B stages are equal
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t bdesc = sdesc_sw128(bbase + ks * 2048, Cfg::BOX64, 1024);
-            if (ti.dw)
-              umma2_ss(dcol, sdesc_sw128(abase + ks * 32, 16, 1024), bdesc, id_dw, (kb | ks) ? 1u : 0u);
-            else
-              umma2_ss(dcol, sdesc_sw128(abase + ks * 2048, Cfg::BOX64, 1024), bdesc, id_dh, (kb | ks) ? 1u : 0u);
+          for (int k8 = 0; k8 < 8; ++k8) {
+            const uint64_t half = static_cast<uint64_t>((k8 >> 2) * (Cfg::HALF >> 4));
+            umma2_ss(dcol, da + so + half + (k8 & 3) * a_step, db_mn + so + half + (k8 & 3) * (2048u >> 4), id,
+                     (kb | k8) ? 1u : 0u);
           }
           umma2_commit_mc(&empty[stage], 3);
           if (++stage == NS) {
@@ -292,7 +302,7 @@ static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pair
 
 cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs,
                                cudaStream_t st) {
-  return bf16 ? launch<true, 6>(maps, prm, max_pairs, st) : launch<false, 6>(maps, prm, max_pairs, st);
+  return bf16 ? launch<true, 3>(maps, prm, max_pairs, st) : launch<false, 3>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc
