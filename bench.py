@@ -58,15 +58,22 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms; ``summary`` keeps the samples
+    taken between ``mark_start`` and ``mark_end`` (the timed region).  ``__enter__`` waits for the
+    first sample so that even a short timed region is covered."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = str(gpu_index)
+    def __init__(self, device):
+        # nvidia-smi numbers GPUs by PCI order, which need not match CUDA's: select by UUID
+        try:
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.gpu = str(device.index)
         self.proc = None
+        self.t0 = self.t1 = None
         self.out = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
 
     def __enter__(self):
@@ -74,13 +81,23 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.out), exist_ok=True)
             self.f = open(self.out, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", self.gpu, "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-i", self.gpu, "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 10.0
+            while time.time() < deadline and self.proc.poll() is None and os.path.getsize(self.out) == 0:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.15)  # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -89,6 +106,14 @@ class ClockSampler:
             self.f.close()
         return False
 
+    @staticmethod
+    def _when(stamp):
+        import datetime
+        try:
+            return datetime.datetime.strptime(stamp, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
     def summary(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -96,16 +121,21 @@ class ClockSampler:
         with open(self.out) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9 and parts[1].isdigit():
+                if len(parts) >= 10 and parts[2].isdigit():
                     rows.append(parts)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [int(r[1]) for r in rows]
+        inside = []
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if (w := self._when(r[0])) is not None and self.t0 - 0.1 <= w <= self.t1 + 0.1]
+        window = inside or rows
+        sm = [int(r[2]) for r in window]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "samples": len(rows),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
-                "reasons": reasons}
+        reasons = sorted({n for r in window for n, v in zip(names, r[6:10]) if v.lower() == "active"})
+        power = [float(r[4]) for r in window if r[4].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(window[0][3]), "samples": len(window),
+                "in_timed_region": bool(inside),
+                "power_w_max": max(power) if power else None, "reasons": reasons}
 
 
 def make_inputs(c, device, rank, world):
@@ -166,12 +196,15 @@ def run_ours(args, c, rank, world, device):
     # ---------------------------------------------------------------- device-resident timing
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clocks, _native.profile() as prof:
+    with ClockSampler(device) as clocks, _native.profile() as prof:
+        barrier()
+        clocks.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
             step(h, t, w)
         ev1.record(stream)
         barrier()
+        clocks.mark_end()
     ms = ev0.elapsed_time(ev1) / args.steps
     peak_gib = (torch.cuda.max_memory_allocated(device) - base) / 2 ** 30
     _native.check_device_error()

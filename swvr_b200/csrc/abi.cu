@@ -176,22 +176,23 @@ static int validate(const swvr_problem* p) {
 
 // ---------------------------------------------------------------------------- forward plan
 struct FwdPlan {
-  int DP, BV, MT, VT, splits, per, units, grid;
+  int MT, VT, splits, per, units, pairs;
   size_t off_m2, off_l, off_acc, bytes;
 };
 
-static FwdPlan plan_fwd(const swvr_problem& p) {
+// Work units are (256-token tile, vocabulary split) pairs run by CTA pairs; the split count
+// minimises the rounds over the co-resident pairs times the tiles per unit.  max_splits
+// bounds the partial-state slots (units * 256 rows).
+static FwdPlan plan_fwd_units(const swvr_problem& p, int max_splits) {
   FwdPlan f{};
-  const int sms = num_sms();
-  f.DP = p.embed_dim <= 64 ? 64 : 128;
-  f.BV = tc::fwd_vocab_tile(f.DP);
-  f.MT = static_cast<int>(ceil_div(p.n_tokens, 128));
-  f.VT = static_cast<int>(ceil_div(p.vocab, f.BV));
+  f.pairs = std::max(1, num_sms() / 2);
+  f.MT = static_cast<int>(ceil_div(p.n_tokens, tc::kFwdTokenTile));
+  f.VT = static_cast<int>(ceil_div(p.vocab, tc::kFwdVocabTile));
   int best_s = 1;
   int64_t best_cost = -1;
-  const int smax = std::max(1, std::min(f.VT, 64));
+  const int smax = std::max(1, std::min(std::min(f.VT, 64), max_splits));
   for (int s = 1; s <= smax; ++s) {
-    const int64_t cost = ceil_div(static_cast<int64_t>(f.MT) * s, sms) * ceil_div(f.VT, s);
+    const int64_t cost = ceil_div(static_cast<int64_t>(f.MT) * s, f.pairs) * ceil_div(f.VT, s);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best_s = s;
@@ -200,8 +201,7 @@ static FwdPlan plan_fwd(const swvr_problem& p) {
   f.per = static_cast<int>(ceil_div(std::max(f.VT, 1), best_s));
   f.splits = static_cast<int>(ceil_div(std::max(f.VT, 1), f.per));
   f.units = f.MT * f.splits;
-  f.grid = std::max(1, std::min(f.units, sms));
-  const size_t rows = static_cast<size_t>(f.units) * 128;
+  const size_t rows = static_cast<size_t>(f.units) * tc::kFwdTokenTile;
   f.off_m2 = 0;
   f.off_l = align_up(rows * 4, 256);
   f.off_acc = f.off_l + align_up(rows * 4, 256);
@@ -209,17 +209,17 @@ static FwdPlan plan_fwd(const swvr_problem& p) {
   return f;
 }
 
-static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo, void* acco, void* ws, size_t wsb,
-                  cudaStream_t st) {
-  const FwdPlan f = plan_fwd(p);
-  if (wsb < f.bytes) return fail(SWVR_ERR_WORKSPACE, "forward workspace %zu < required %zu", wsb, f.bytes);
-  if (p.n_tokens == 0) return SWVR_OK;
+static FwdPlan plan_fwd(const swvr_problem& p) { return plan_fwd_units(p, 64); }
+
+// Tensor maps and kernel parameters of the tensor-core forward; the caller provides the
+// partial-state scratch (f.bytes).
+static int tc_fwd_launch(const swvr_problem& p, const FwdPlan& f, char* scratch, cudaStream_t st,
+                         tc::FwdParams* out) {
   const bool bf16 = p.compute_dtype == SWVR_BF16;
   tc::FwdMaps maps;
   SWVR_TRY(make_map(&maps.h, p.h, p.compute_dtype, p.hidden, p.n_tokens, p.ldh * 2, 64, 128));
-  SWVR_TRY(make_map(&maps.w, p.W, p.compute_dtype, p.hidden, p.vocab, p.ldw * 2, 64, f.BV));
-  SWVR_TRY(make_map(&maps.e, p.E, p.compute_dtype, p.embed_dim, p.vocab, p.lde * 2, 64, f.BV));
-  char* w = static_cast<char*>(ws);
+  SWVR_TRY(make_map(&maps.w, p.W, p.compute_dtype, p.hidden, p.vocab, p.ldw * 2, 64, tc::kFwdVocabTile / 2));
+  SWVR_TRY(make_map(&maps.e, p.E, p.compute_dtype, p.embed_dim, p.vocab, p.lde * 2, 64, tc::kFwdVocabTile));
   tc::FwdParams prm{};
   prm.N = static_cast<int>(p.n_tokens);
   prm.K = static_cast<int>(p.hidden);
@@ -233,17 +233,28 @@ static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo
   prm.splits = f.splits;
   prm.per = f.per;
   prm.units = f.units;
-  prm.part_m2 = reinterpret_cast<float*>(w + f.off_m2);
-  prm.part_l = reinterpret_cast<float*>(w + f.off_l);
-  prm.part_acc = reinterpret_cast<float*>(w + f.off_acc);
-  if (p.vocab == 0) return fail(SWVR_ERR_UNSUPPORTED, "empty vocabulary (callers handle V == 0)");
+  prm.part_m2 = reinterpret_cast<float*>(scratch + f.off_m2);
+  prm.part_l = reinterpret_cast<float*>(scratch + f.off_l);
+  prm.part_acc = reinterpret_cast<float*>(scratch + f.off_acc);
   {
     ProfScope ps(kProfFwd, st);
-    SWVR_CUDA(tc::launch_fwd_kernel(bf16, f.DP, maps, prm, f.grid, st));
+    SWVR_CUDA(tc::launch_fwd_kernel(bf16, maps, prm, f.pairs, st));
   }
+  *out = prm;
+  return SWVR_OK;
+}
+
+static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo, void* acco, void* ws, size_t wsb,
+                  cudaStream_t st) {
+  const FwdPlan f = plan_fwd(p);
+  if (wsb < f.bytes) return fail(SWVR_ERR_WORKSPACE, "forward workspace %zu < required %zu", wsb, f.bytes);
+  if (p.n_tokens == 0) return SWVR_OK;
+  if (p.vocab == 0) return fail(SWVR_ERR_UNSUPPORTED, "empty vocabulary (callers handle V == 0)");
+  tc::FwdParams prm;
+  SWVR_TRY(tc_fwd_launch(p, f, static_cast<char*>(ws), st, &prm));
   ProfScope ps_c(kProfCombine, st);
   SWVR_CUDA(small::combine(SWVR_F32, f.splits, p.n_tokens, p.embed_dim, prm.part_m2, prm.part_l, prm.part_acc, 0,
-                           f.splits, O, lse, m2o, lo, acco, st));
+                           f.splits, tc::kFwdTokenTile, O, lse, m2o, lo, acco, st));
   return SWVR_OK;
 }
 
@@ -536,7 +547,7 @@ int swvr_combine(int64_t shards, int64_t n_tokens, int64_t embed_dim, int32_t ac
   if (acc_dt != SWVR_F32 && acc_dt != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "combine dtype must be F32/F64");
   if (n_tokens > 0 && (!m2 || !l || !acc || !O || !lse)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
   ProfScope ps(kProfCombine, static_cast<cudaStream_t>(stream));
-  SWVR_CUDA(small::combine(acc_dt, static_cast<int>(shards), n_tokens, embed_dim, m2, l, acc, 1, 1, O, lse, nullptr,
+  SWVR_CUDA(small::combine(acc_dt, static_cast<int>(shards), n_tokens, embed_dim, m2, l, acc, 1, 1, 0, O, lse, nullptr,
                            nullptr, nullptr, static_cast<cudaStream_t>(stream)));
   return SWVR_OK;
 }

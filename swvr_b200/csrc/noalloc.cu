@@ -57,39 +57,16 @@ static int fwd_scratch_address(void** out) {
 
 // The forward plan restricted to the static scratch: as many vocabulary splits as fit.
 static int plan_fwd_static(const swvr_problem& p, FwdPlan* out) {
-  FwdPlan f{};
-  const int sms = num_sms();
-  f.DP = p.embed_dim <= 64 ? 64 : 128;
-  f.BV = tc::fwd_vocab_tile(f.DP);
-  f.MT = static_cast<int>(ceil_div(p.n_tokens, 128));
-  f.VT = static_cast<int>(ceil_div(p.vocab, f.BV));
-  const size_t per_unit = align_up(128 * 4, 256) * 2 + align_up(size_t(128) * p.embed_dim * 4, 256);
+  const size_t per_unit = align_up(tc::kFwdTokenTile * 4, 256) * 2 + align_up(size_t(tc::kFwdTokenTile) * p.embed_dim * 4, 256);
   const size_t max_units = (kFwdScratchBytes - 3 * 256) / per_unit;
-  if (static_cast<size_t>(f.MT) > max_units)
+  const int64_t MT = ceil_div(p.n_tokens, tc::kFwdTokenTile);
+  if (static_cast<size_t>(MT) > max_units)
     return fail(SWVR_ERR_UNSUPPORTED,
                 "swvr_fwd_noalloc: N=%lld, D=%lld needs %zu bytes of scratch even unsplit; the static scratch holds "
-                "%zu bytes (at most %zu 128-token tiles of this D)",
-                (long long)p.n_tokens, (long long)p.embed_dim, static_cast<size_t>(f.MT) * per_unit, kFwdScratchBytes,
-                max_units);
-  const int smax = std::max(1, std::min<int>(std::min(f.VT, 64), static_cast<int>(max_units / f.MT)));
-  int best_s = 1;
-  int64_t best_cost = -1;
-  for (int s = 1; s <= smax; ++s) {
-    const int64_t cost = ceil_div(static_cast<int64_t>(f.MT) * s, sms) * ceil_div(f.VT, s);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best_s = s;
-    }
-  }
-  f.per = static_cast<int>(ceil_div(std::max(f.VT, 1), best_s));
-  f.splits = static_cast<int>(ceil_div(std::max(f.VT, 1), f.per));
-  f.units = f.MT * f.splits;
-  f.grid = std::max(1, std::min(f.units, sms));
-  const size_t rows = static_cast<size_t>(f.units) * 128;
-  f.off_m2 = 0;
-  f.off_l = align_up(rows * 4, 256);
-  f.off_acc = f.off_l + align_up(rows * 4, 256);
-  f.bytes = f.off_acc + align_up(rows * p.embed_dim * 4, 256);
+                "%zu bytes (at most %zu %d-token tiles of this D)",
+                (long long)p.n_tokens, (long long)p.embed_dim, static_cast<size_t>(MT) * per_unit, kFwdScratchBytes,
+                max_units, tc::kFwdTokenTile);
+  const FwdPlan f = plan_fwd_units(p, static_cast<int>(max_units / static_cast<size_t>(MT)));
   if (f.bytes > kFwdScratchBytes)
     return fail(SWVR_ERR_UNSUPPORTED, "swvr_fwd_noalloc: plan needs %zu bytes of scratch, the static scratch holds %zu",
                 f.bytes, kFwdScratchBytes);
@@ -112,34 +89,10 @@ extern "C" int swvr_fwd_noalloc(const swvr_problem* p, void* O, void* lse, void*
   void* scratch = nullptr;
   SWVR_TRY(fwd_scratch_address(&scratch));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool bf16 = p->compute_dtype == SWVR_BF16;
-  tc::FwdMaps maps;
-  SWVR_TRY(make_map(&maps.h, p->h, p->compute_dtype, p->hidden, p->n_tokens, p->ldh * 2, 64, 128));
-  SWVR_TRY(make_map(&maps.w, p->W, p->compute_dtype, p->hidden, p->vocab, p->ldw * 2, 64, f.BV));
-  SWVR_TRY(make_map(&maps.e, p->E, p->compute_dtype, p->embed_dim, p->vocab, p->lde * 2, 64, f.BV));
-  char* w = static_cast<char*>(scratch);
-  tc::FwdParams prm{};
-  prm.N = static_cast<int>(p->n_tokens);
-  prm.K = static_cast<int>(p->hidden);
-  prm.V = static_cast<int>(p->vocab);
-  prm.D = static_cast<int>(p->embed_dim);
-  prm.sc2 = static_cast<float>(p->logit_scale * 1.4426950408889634);
-  prm.bias = p->bias;
-  prm.bias_dt = p->bias_dtype;
-  prm.MT = f.MT;
-  prm.VT = f.VT;
-  prm.splits = f.splits;
-  prm.per = f.per;
-  prm.units = f.units;
-  prm.part_m2 = reinterpret_cast<float*>(w + f.off_m2);
-  prm.part_l = reinterpret_cast<float*>(w + f.off_l);
-  prm.part_acc = reinterpret_cast<float*>(w + f.off_acc);
-  {
-    ProfScope ps(kProfFwd, st);
-    SWVR_CUDA(tc::launch_fwd_kernel(bf16, f.DP, maps, prm, f.grid, st));
-  }
+  tc::FwdParams prm;
+  SWVR_TRY(tc_fwd_launch(*p, f, static_cast<char*>(scratch), st, &prm));
   ProfScope ps_c(kProfCombine, st);
   SWVR_CUDA(small::combine(SWVR_F32, f.splits, p->n_tokens, p->embed_dim, prm.part_m2, prm.part_l, prm.part_acc, 0,
-                           f.splits, O, lse, nullptr, nullptr, nullptr, st));
+                           f.splits, tc::kFwdTokenTile, O, lse, nullptr, nullptr, nullptr, st));
   return SWVR_OK;
 }

@@ -10,14 +10,15 @@ namespace swvr {
 namespace small {
 
 // ------------------------------------------------------------------ combine
-// Source s of row n lives at idx(s, n): split slots of the tensor-core forward
-// (mode 0: ((n/128)*splits + s)*128 + n%128) or shard-major arrays (mode 1: s*N + n).
+// Source s of row n lives at idx(s, n): split slots of the tensor-core forward (mode 0,
+// T = tile_rows: ((n/T)*splits + s)*T + n%T) or shard-major arrays (mode 1: s*N + n).
 template <typename T>
 __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict__ m2, const T* __restrict__ l,
-                               const T* __restrict__ acc, int mode, int splits, T* O, T* lse, T* m2o, T* lo, T* acco) {
+                               const T* __restrict__ acc, int mode, int splits, int tile_rows, T* O, T* lse, T* m2o,
+                               T* lo, T* acco) {
   const int64_t n = blockIdx.x;
   auto idx = [&](int s) -> int64_t {
-    return mode == 0 ? ((n / 128) * splits + s) * 128 + (n % 128) : static_cast<int64_t>(s) * N + n;
+    return mode == 0 ? ((n / tile_rows) * splits + s) * tile_rows + (n % tile_rows) : static_cast<int64_t>(s) * N + n;
   };
   double M = -INFINITY;
   for (int s = 0; s < S; ++s) M = fmax(M, static_cast<double>(m2[idx(s)]));
@@ -44,18 +45,18 @@ __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict_
 }
 
 cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
-                    int splits, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st) {
+                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
   if (acc_dt == SWVR_F64)
     combine_kernel<double><<<static_cast<unsigned>(N), threads, 0, st>>>(
         S, N, D, static_cast<const double*>(m2), static_cast<const double*>(l), static_cast<const double*>(acc), mode,
-        splits, static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
+        splits, tile_rows, static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
         static_cast<double*>(lo), static_cast<double*>(acco));
   else
     combine_kernel<float><<<static_cast<unsigned>(N), threads, 0, st>>>(
         S, N, D, static_cast<const float*>(m2), static_cast<const float*>(l), static_cast<const float*>(acc), mode,
-        splits, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o), static_cast<float*>(lo),
+        splits, tile_rows, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o), static_cast<float*>(lo),
         static_cast<float*>(acco));
   return cudaGetLastError();
 }

@@ -5,7 +5,7 @@
 namespace swvr {
 namespace small {
 cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
-                    int splits, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st);
+                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st);
 cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
                          int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt,
                          cudaStream_t st);

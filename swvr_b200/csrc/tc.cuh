@@ -14,19 +14,24 @@ struct FwdParams {
   float sc2;  // logit_scale * log2(e)
   const void* bias;
   int bias_dt;
-  int MT, VT;             // 128-token tiles, vocabulary tiles
+  int MT, VT;             // 256-token pair tiles, vocabulary tiles
   int splits, per, units; // vocabulary splits per token tile, tiles per split, MT * splits
-  float* part_m2;         // [units * 128]
-  float* part_l;          // [units * 128]
-  float* part_acc;        // [units * 128 * D]
+  float* part_m2;         // [units * 256]
+  float* part_l;          // [units * 256]
+  float* part_acc;        // [units * 256 * D]
 };
+
+constexpr int kFwdTokenTile = 256;  // tokens per work unit (a CTA pair, 128 per CTA)
+constexpr int kFwdVocabTile = 192;  // vocabulary rows per tile
 
 struct FwdMaps {
-  CUtensorMap h, w, e;
+  CUtensorMap h;  // h, box {64, 128}
+  CUtensorMap w;  // W, box {64, 96} (half a vocabulary tile)
+  CUtensorMap e;  // E, box {64, 192}
 };
 
-int fwd_vocab_tile(int DP);
-cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int grid, cudaStream_t st);
+// Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
+cudaError_t launch_fwd_kernel(bool bf16, const FwdMaps& maps, const FwdParams& prm, int max_pairs, cudaStream_t st);
 
 // ------------------------------------------------------------------ backward: scores tile kernel
 struct BwdScoresParams {

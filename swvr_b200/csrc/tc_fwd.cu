@@ -1,17 +1,22 @@
-// Tensor-core (tcgen05) forward of the softmax readout on sm_100a.
+// Tensor-core (tcgen05) forward of the softmax readout on sm_100a, 2-SM.
 //
-// One CTA per SM walks work units (a 128-token tile x a contiguous range of vocabulary
-// tiles).  Per vocabulary tile j:
-//   S_j  = h_tile . W_j^T            tcgen05.mma, A/B from 128B-swizzled smem, D in TMEM
+// A CTA pair (cluster of 2) walks work units (a 256-token tile x a contiguous range of
+// 192-row vocabulary tiles).  Each CTA owns 128 of the tokens (TMEM lanes = token rows).
+// Per vocabulary tile j, with tcgen05.mma.cta_group::2 issued by the even CTA:
+//   S_j  = h_tile . W_j^T            M = 256 tokens, N = 192 rows; each CTA stages its own
+//                                    128 h rows and half (96) of the W rows per K-block
 //   P_j  = 2^(S_j*s*log2e + b*log2e - m_ref), rounded to bf16/fp16 and stored back into
-//          TMEM over S_j
-//   O   += P_j . E_j                 tcgen05.mma with A read from TMEM
-// so neither S nor P ever leaves the SM.  Warp roles: warp 0 issues TMA loads, warp 1
-// (one thread) issues MMAs, warps 4-7 run the online softmax with one thread per token
-// row (TMEM lane = row, so row max / row sum are thread-local).  S is double-buffered in
-// TMEM, so the MMAs of tile j+1 overlap the softmax of tile j.  The running reference max
-// m_ref is only raised when a tile's max exceeds it by more than 2^8 (the result is
-// exact either way because l and O share m_ref); then O is rescaled in TMEM.
+//          TMEM over S_j (one thread per token row: row max / row sum are thread-local)
+//   O   += P_j . E_j                 A = P from TMEM; B = E_j, N = 128 (each CTA stages 64
+//                                    embedding columns; past D the boxes read zero fill)
+// so neither S nor P ever leaves the SM.  A pair moves 28 KB per CTA per 64-wide K-block
+// for 2*256*192*64 FLOP, against 40 KB for a single-CTA 128x192 tile: the L2->SMEM feed,
+// which bounds the single-CTA kernel, drops below the MMA rate.  Warp roles: warp 0 issues
+// TMA loads, warp 1 (one thread, even CTA) issues MMAs, warps 4-7 run the online softmax.
+// S is double-buffered in TMEM (2 x 192 columns, O in the last 128), so the MMAs of tile
+// j+1 overlap the softmax of tile j.  The running reference max m_ref is only raised when
+// a chunk's max exceeds it by more than 2^kEmergency (exact either way because l and O
+// share m_ref); then O is rescaled in TMEM.
 //
 // Each unit writes its per-row state (m_ref in log2 units, l, O-accumulator) to a partial
 // slot; combine_kernel (small.cu) merges the slots of a row in a fixed order.
@@ -24,49 +29,57 @@
 namespace swvr {
 namespace tc {
 
-template <bool kBF16, int BV, int DP, int NS>
+// KH: 64-wide K halves per pipeline stage (8 MMAs per barrier round trip of the MMA thread).
+template <bool kBF16, int NS, int KH>
 struct FwdCfg {
-  static constexpr int BM = 128, BK = 64;
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BV * BK * 2;
-  static constexpr int E_BOX = BV * 128;  // one 64-column box of the E tile
-  static constexpr int E_BYTES = (DP / 64) * E_BOX;
+  static constexpr int BV = kFwdVocabTile;   // vocabulary rows per tile (MMA N)
+  static constexpr int HBV = BV / 2;         // W rows staged by each CTA
+  static constexpr int BOXA = 128 * 128;     // 128 h rows x 64 K
+  static constexpr int BOXB = HBV * 128;     // 96 W rows x 64 K
+  static constexpr int A_BYTES = KH * BOXA;
+  static constexpr int B_BYTES = KH * BOXB;
+  static constexpr int E_BYTES = BV * 128;   // 192 vocabulary rows x this CTA's 64 embedding columns
   static constexpr int SMEM_A = 0;
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
   static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
   static constexpr int SMEM_BIAS = SMEM_E + 2 * E_BYTES;  // 2 x 256 floats: bias*log2e, -inf past V
   static constexpr int SMEM_BAR = SMEM_BIAS + 2 * 256 * 4;
-  static constexpr int NBAR = 2 * NS + 11;  // last one: abort drain
+  static constexpr int NBAR = 2 * NS + 12;
   static constexpr float kEmergency = kBF16 ? 64.f : 8.f;  // max P = 2^kEmergency stays finite in 16 bits
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
-  static constexpr uint32_t O_COL = 2 * BV;
-  static_assert(2 * BV + DP <= 512, "TMEM budget");
-  static_assert(BV % 32 == 0 && BV <= 256, "vocab tile");
+  static constexpr uint32_t O_COL = 2 * BV;  // O: 128 columns (N = 128: 64 embedding columns per CTA)
+  static_assert(O_COL + 128 <= 512, "TMEM budget");
+  static_assert(BV % 32 == 0 && HBV % 8 == 0, "vocabulary tile");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
-  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0 && E_BOX % 1024 == 0, "1024-byte alignment");
+  static_assert(BOXA % 1024 == 0 && BOXB % 1024 == 0 && E_BYTES % 1024 == 0, "1024-byte alignment");
 };
 
-template <bool kBF16, int BV, int DP, int NS>
+template <bool kBF16, int NS, int KH>
 __global__ void __launch_bounds__(256, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_w,
                const __grid_constant__ CUtensorMap tm_e, const FwdParams p) {
-  using Cfg = FwdCfg<kBF16, BV, DP, NS>;
+  using Cfg = FwdCfg<kBF16, NS, KH>;
+  constexpr int BV = Cfg::BV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + NS;
-  uint64_t* s_full = bars + 2 * NS;
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* e_full = p_ready + 2;
-  uint64_t* e_empty = e_full + 2;
-  uint64_t* pe_done = e_empty + 2;
-  uint64_t* o_free = pe_done + 1;
+  uint64_t* full = bars;              // [NS] leader: both CTAs' bytes
+  uint64_t* empty = bars + NS;        // [NS] both (multicast commit)
+  uint64_t* s_full = bars + 2 * NS;   // [2] both
+  uint64_t* p_ready = s_full + 2;     // [2] leader: one arrival per CTA
+  uint64_t* e_full = p_ready + 2;     // [2] leader: both CTAs' bytes
+  uint64_t* e_empty = e_full + 2;     // [2] both
+  uint64_t* pe_done = e_empty + 2;    // both
+  uint64_t* o_free = pe_done + 1;     // leader: one arrival per CTA
+  uint64_t* spare = o_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
@@ -74,13 +87,13 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_ready[b], 128);
+      mbar_init(&p_ready[b], 2);
       mbar_init(&e_full[b], 1);
       mbar_init(&e_empty[b], 1);
     }
     mbar_init(pe_done, 1);
-    mbar_init(o_free, 128);
-    mbar_init(&bars[Cfg::NBAR - 1], 1);
+    mbar_init(o_free, 2);
+    mbar_init(spare, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -90,28 +103,36 @@ __global__ void __launch_bounds__(256, 1)
     tma_prefetch_desc(&tm_e);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_holder, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int KB = (p.K + 63) / 64;
+  const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
+      // ------------------------------------------------------------ TMA producer (both CTAs)
       uint32_t stage = 0, sphase = 0, g = 0;
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      for (int u = pair; u < p.units; u += npairs) {
         const int mt = u / p.splits, sp = u % p.splits;
         const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
+        const int hrow = mt * 256 + static_cast<int>(rank) * 128;
         for (int vt = vt0; vt < vt1; ++vt, ++g) {
+          const int wrow = vt * BV + static_cast<int>(rank) * Cfg::HBV;
           for (int kb = 0; kb < KB; ++kb) {
             if (!mbar_wait(&empty[stage], sphase ^ 1u, abort_flag, kErrFwd | 1)) goto done;
-            mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
-            tma_load_2d(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES, &tm_h, &full[stage], kb * 64, mt * 128);
-            tma_load_2d(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES, &tm_w, &full[stage], kb * 64, vt * BV);
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+#pragma unroll
+            for (int hk = 0; hk < KH; ++hk) {
+              const int k0 = (kb * KH + hk) * 64;  // past K the boxes read zero fill
+              tma_load_2d_pair(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES + hk * Cfg::BOXA, &tm_h, fb, k0, hrow);
+              tma_load_2d_pair(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES + hk * Cfg::BOXB, &tm_w, fb, k0, wrow);
+            }
             if (++stage == NS) {
               stage = 0;
               sphase ^= 1u;
@@ -119,20 +140,22 @@ __global__ void __launch_bounds__(256, 1)
           }
           const uint32_t eb = g & 1u, use = g >> 1;
           if (!mbar_wait(&e_empty[eb], (use & 1u) ^ 1u, abort_flag, kErrFwd | 2)) goto done;
-          mbar_arrive_expect_tx(&e_full[eb], Cfg::E_BYTES);
-#pragma unroll
-          for (int c = 0; c < DP / 64; ++c)
-            tma_load_2d(smem + Cfg::SMEM_E + eb * Cfg::E_BYTES + c * Cfg::E_BOX, &tm_e, &e_full[eb], c * 64, vt * BV);
+          if (leader) mbar_arrive_expect_tx(&e_full[eb], 2 * Cfg::E_BYTES);
+          tma_load_2d_pair(smem + Cfg::SMEM_E + eb * Cfg::E_BYTES, &tm_e, mapa_shared(smem_u32(&e_full[eb]), 0),
+                           static_cast<int>(rank) * 64, vt * BV);
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      const uint32_t idS = idesc_f16(kBF16, 128, BV, false, false);
-      const uint32_t idPE = idesc_f16(kBF16, 128, DP, false, true);
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      const uint32_t idS = idesc_f16(kBF16, 256, BV, false, false);
+      const uint32_t idPE = idesc_f16(kBF16, 256, 128, false, true);
+      // stage-0 descriptors; a stage / K half / 16-wide K step adds (byte offset >> 4)
+      const uint64_t da0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);
+      const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
-      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      for (int u = pair; u < p.units; u += npairs) {
         const int sp = u % p.splits;
         const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
         const int ntiles = vt1 - vt0;
@@ -142,20 +165,19 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t b = g & 1u;
             for (int kb = 0; kb < KB; ++kb) {
               if (!mbar_wait(&full[stage], sphase, abort_flag, kErrFwd | 3)) goto done;
-              tc_fence_after();
-              const uint32_t abase = smem_u32(smem + Cfg::SMEM_A + stage * Cfg::A_BYTES);
-              const uint32_t bbase = smem_u32(smem + Cfg::SMEM_B + stage * Cfg::B_BYTES);
+              const uint64_t sa = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));
+              const uint64_t sb = static_cast<uint64_t>(stage * (Cfg::B_BYTES >> 4));
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks)
-                umma_ss(tmem + b * BV, sdesc_sw128(abase + ks * 32, 16, 1024), sdesc_sw128(bbase + ks * 32, 16, 1024),
-                        idS, (kb | ks) ? 1u : 0u);
-              umma_commit(&empty[stage]);
+              for (int k8 = 0; k8 < 4 * KH; ++k8)
+                umma2_ss(tmem + b * BV, da0 + sa + (k8 >> 2) * (Cfg::BOXA >> 4) + (k8 & 3) * 2,
+                         db0 + sb + (k8 >> 2) * (Cfg::BOXB >> 4) + (k8 & 3) * 2, idS, (kb | k8) ? 1u : 0u);
+              umma2_commit_mc(&empty[stage], 3);
               if (++stage == NS) {
                 stage = 0;
                 sphase ^= 1u;
               }
             }
-            umma_commit(&s_full[b]);
+            umma2_commit_mc(&s_full[b], 3);
             ++g;
           }
           if (j > 0) {
@@ -170,31 +192,33 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E + bb * Cfg::E_BYTES);
 #pragma unroll
             for (int ks = 0; ks < BV / 16; ++ks)
-              umma_ts(tmem + Cfg::O_COL, tmem + bb * BV + ks * 8, sdesc_sw128(ebase + ks * 2048, Cfg::E_BOX, 1024),
-                      idPE, (first && ks == 0) ? 0u : 1u);
-            umma_commit(pe_done);
-            umma_commit(&e_empty[bb]);
+              umma2_ts(tmem + Cfg::O_COL, tmem + bb * BV + ks * 8, sdesc_sw128(ebase + ks * 2048, Cfg::E_BYTES, 1024),
+                       idPE, (first && ks == 0) ? 0u : 1u);
+            umma2_commit_mc(pe_done, 3);
+            umma2_commit_mc(&e_empty[bb], 3);
           }
         }
         ++uc;
       }
     }
   } else if (warp >= 4) {
-    // -------------------------------------------------------------- softmax warps
-    // One pass per tile.  P = 2^(t - ref) with t = S*s*log2e + b*log2e and ref an integer
-    // reference max (so every rescale factor is an exact power of two).  A 32-column chunk
-    // whose max exceeds ref + kEmergency raises ref to ceil(max) and rescales the P chunks
-    // of this tile already in TMEM, l, and (after the previous P.E completed) O.
+    // -------------------------------------------------------------- softmax warps (both CTAs)
+    // One pass per tile.  P = 2^(t - ref) with t = S*s*log2e + b*log2e and ref the running
+    // reference max.  A 32-column chunk whose max exceeds ref + kEmergency raises ref to
+    // that max and rescales the P chunks of this tile already in TMEM, l, and (after the
+    // previous P.E completed) O.
     const int r = threadIdx.x - 128;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t trow = tmem + lane_base;
     float* bias_s = reinterpret_cast<float*>(smem + Cfg::SMEM_BIAS);
+    const uint32_t p_ready_leader = mapa_shared(smem_u32(p_ready), 0);
+    const uint32_t o_free_leader = mapa_shared(smem_u32(o_free), 0);
     uint32_t g = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+    for (int u = pair; u < p.units; u += npairs) {
       const int mt = u / p.splits, sp = u % p.splits;
       const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
       if (vt1 <= vt0) continue;
-      const int n = mt * 128 + r;
+      const int n = mt * 256 + static_cast<int>(rank) * 128 + r;
       float ref = -INFINITY, l = 0.f;
       for (int vt = vt0; vt < vt1; ++vt, ++g) {
         const uint32_t b = g & 1u;
@@ -274,40 +298,42 @@ __global__ void __launch_bounds__(256, 1)
           if (__any_sync(0xffffffffu, ref != ref_start)) {
             const float alpha = ref == ref_start ? 1.f : ex2(ref_start - ref);
 #pragma unroll 1
-            for (int c = 0; c < DP / 32; ++c) {
+            for (int c = 0; c < p.D; c += 32) {
               uint32_t o[32];
-              tmem_ld32(trow + Cfg::O_COL + c * 32, o);
+              tmem_ld32(trow + Cfg::O_COL + c, o);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(trow + Cfg::O_COL + c * 32, o);
+              tmem_st32(trow + Cfg::O_COL + c, o);
             }
           }
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_ready[b]);
+        named_bar_sync(1, 128);
+        if (r == 0) mbar_arrive_cluster(p_ready_leader + b * 8);
       }
       // unit end: wait for the last P.E, then write this unit's partial state
       if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 9)) goto done;
       tc_fence_after();
       {
-        const int64_t slot = static_cast<int64_t>(u) * 128 + r;
+        const int64_t slot = static_cast<int64_t>(u) * 256 + static_cast<int>(rank) * 128 + r;
 #pragma unroll 1
-        for (int c = 0; c < DP / 32; ++c) {
+        for (int c = 0; c < p.D; c += 32) {
           uint32_t o[32];
-          tmem_ld32(trow + Cfg::O_COL + c * 32, o);
+          tmem_ld32(trow + Cfg::O_COL + c, o);
           tmem_wait_ld();
           if (n < p.N) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const int d = c * 32 + i;
+              const int d = c + i;
               if (d < p.D) p.part_acc[slot * p.D + d] = __uint_as_float(o[i]);
             }
           }
         }
         tc_fence_before();
-        mbar_arrive(o_free);
+        named_bar_sync(1, 128);
+        if (r == 0) mbar_arrive_cluster(o_free_leader);
         if (n < p.N) {
           p.part_m2[slot] = ref;
           p.part_l[slot] = l;
@@ -318,32 +344,44 @@ __global__ void __launch_bounds__(256, 1)
 done:
   tc_fence_before();
   __syncthreads();
-  if (*abort_flag) drain_after_abort(warp == 1 && lane == 0, &bars[Cfg::NBAR - 1]);
+  if (*abort_flag) drain_after_abort_pair(warp == 1 && lane == 0 && leader, spare);
+  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
 // ------------------------------------------------------------------------------------- host
-template <bool kBF16, int BV, int DP, int NS>
-static cudaError_t launch_fwd(const FwdMaps& maps, const FwdParams& prm, int grid, cudaStream_t st) {
-  using Cfg = FwdCfg<kBF16, BV, DP, NS>;
-  auto kern = fwd_kernel<kBF16, BV, DP, NS>;
+template <bool kBF16, int NS, int KH>
+static cudaError_t launch_fwd(const FwdMaps& m, const FwdParams& prm, int max_pairs, cudaStream_t st) {
+  using Cfg = FwdCfg<kBF16, NS, KH>;
+  auto kern = fwd_kernel<kBF16, NS, KH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
-  kern<<<grid, 256, Cfg::SMEM_ALLOC, st>>>(maps.h, maps.w, maps.e, prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+  cfg.stream = st;
+  cfg.gridDim = dim3(2 * 74, 1, 1);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess) return e;
+  int pairs = std::min(std::min(clusters, max_pairs), prm.units);
+  if (pairs < 1) pairs = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  return cudaLaunchKernelEx(&cfg, kern, m.h, m.w, m.e, prm);
 }
 
-int fwd_vocab_tile(int DP) { return DP <= 64 ? 192 : 160; }
-
-cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int grid,
-                              cudaStream_t st) {
-  if (DP == 64) {
-    return bf16 ? launch_fwd<true, 192, 64, 4>(maps, prm, grid, st) : launch_fwd<false, 192, 64, 4>(maps, prm, grid, st);
-  }
-  return bf16 ? launch_fwd<true, 160, 128, 3>(maps, prm, grid, st) : launch_fwd<false, 160, 128, 3>(maps, prm, grid, st);
+cudaError_t launch_fwd_kernel(bool bf16, const FwdMaps& maps, const FwdParams& prm, int max_pairs, cudaStream_t st) {
+  return bf16 ? launch_fwd<true, 3, 2>(maps, prm, max_pairs, st) : launch_fwd<false, 3, 2>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc
