@@ -124,7 +124,7 @@ static EncodeFn encode_fn() {
 // 2-D row-major tensor [outer, inner] with a row pitch of row_bytes; 128-byte swizzle, zero
 // fill out of bounds.
 static int make_map(CUtensorMap* m, const void* base, int dt, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                    uint32_t box_inner, uint32_t box_outer) {
+                    uint32_t box_inner, uint32_t box_outer, int swizzle_bytes = 128) {
   EncodeFn fn = encode_fn();
   if (!fn) return fail(SWVR_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_bytes & 15u) != 0)
@@ -138,7 +138,8 @@ static int make_map(CUtensorMap* m, const void* base, int dt, uint64_t inner, ui
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   const CUresult r = fn(m, t, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(SWVR_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (%d): dims {%llu, %llu}, pitch %llu, box {%u, %u}",
                 static_cast<int>(r), static_cast<unsigned long long>(inner), static_cast<unsigned long long>(outer),
@@ -360,8 +361,9 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
   SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));
   SWVR_TRY(make_map(&sm.h64, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
   SWVR_TRY(make_map(&sm.e, p.E, p.compute_dtype, D, V, p.lde * 2, 64, 128));
-  SWVR_TRY(make_map(&sm.go64, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 64));
-  SWVR_TRY(make_map(&sm.go128, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 128));
+  SWVR_TRY(make_map(&sm.gok, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 64));
+  const int gomw = tc::bwd_gom_width(b.DP);
+  SWVR_TRY(make_map(&sm.gom, goc, p.compute_dtype, b.DP, N, b.DP * 2, gomw, 128, gomw * 2));
   tc::GemmMaps gm;
   if (b.need_ds) {
     SWVR_TRY(make_map(&gm.h_mn, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
@@ -410,9 +412,6 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     if (b.need_ds) {
       SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
       SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
-      sm.ds = gm.ds_k;
-    } else {
-      sm.ds = sm.go128;  // unused
     }
     {
       ProfScope ps(kProfBwdScores, st);

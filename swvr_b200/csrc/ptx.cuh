@@ -186,6 +186,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// The same for a 64-byte swizzled operand (8-row x 64-byte swizzle atoms of 512 bytes).
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(4) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation:
 //   [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16, 1 = bf16),
 //   [15] A MN-major, [16] B MN-major, [17,23) N >> 3, [24,29) M >> 4.

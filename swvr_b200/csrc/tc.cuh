@@ -44,20 +44,22 @@ struct BwdScoresParams {
   const float* delta;  // [N]
   int NT, VT;          // 128-token tiles, 256-row vocabulary pair tiles of the chunk
   int TS, per_t, units;  // token splits, token tiles per split, VT * TS
-  void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null
+  void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null (ld_ds >= NT*128)
   int64_t ld_ds;
   float* part_de;      // [units * 256 * D] or null
   float* part_db;      // [units * 256] or null
 };
 
 struct BwdScoresMaps {
-  CUtensorMap w;      // W, box {64, 128}
-  CUtensorMap h64;    // h, box {64, 64} (half a token tile)
-  CUtensorMap e;      // E, box {64, 128}
-  CUtensorMap go64;   // gO in the compute dtype [N, DP], box {64, 64}
-  CUtensorMap go128;  // the same, box {64, 128}
-  CUtensorMap ds;     // this chunk's dS^T [rows, Npad], box {64, 128} (TMA store)
+  CUtensorMap w;    // W, box {64, 128}
+  CUtensorMap h64;  // h, box {64, 64} (half a token tile)
+  CUtensorMap e;    // E, box {64, 128}
+  CUtensorMap gok;  // gO in the compute dtype [Npad, DP], box {64, 64}, 128-byte swizzle
+  CUtensorMap gom;  // the same, box {bwd_gom_width(DP), 128}, 64-byte (DP 64) or 128-byte swizzle
 };
+
+// Embedding columns of gO each CTA stages as the MN-major dE operand (half the dE MMA N).
+int bwd_gom_width(int DP);
 
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,

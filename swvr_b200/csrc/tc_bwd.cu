@@ -10,10 +10,15 @@
 //   dS^T * s is stored in the compute dtype for the dh / dW GEMMs (tc_gemm.cu).
 // All three products are tcgen05.mma.cta_group::2 issued by the even CTA: each CTA stages
 // its own 128 W rows and half of the h tile (64 tokens), so a pair moves 24 KB per CTA per
-// K-block for 2*256*128*64 FLOP (87 FLOP/B, against 64 for a single-CTA 128x128 tile).
-// gO is staged twice per token tile: the CTA's 64-token half, K-major, as the B operand of
-// dP^T, and the CTA's 64-column half of all 128 tokens, MN-major, as the B operand of dE
-// (whose N is padded to 128, so for D <= 64 the odd CTA's half is zero fill).
+// 64-wide K-block for 2*256*128*64 FLOP.  The W / h ring has 4 stages of 128-wide K-blocks
+// for D <= 64 (3 for D <= 128): the MMAs of a stage take ~512 cycles and the L2 latency of
+// the TMA loads under load is about three stages of that.
+// gO is staged twice per token tile, each copy single-buffered with its own barriers: the
+// CTA's 64-token half, K-major, as the B operand of dP^T (loaded early in the tile's S
+// K-loop, after the previous dP has completed), and the CTA's half of the embedding
+// columns of all 128 tokens, MN-major, as the B operand of dE (loaded one tile later, after
+// the previous dE).  For D <= 64 dE is N = 64 and the MN-major copy is 32 columns wide with a
+// 64-byte swizzle; for D <= 128 it is N = 128 with a 128-byte swizzle.
 // dE and db of a unit go to a partial slot; reduce_de_db_kernel (small.cu) sums the token
 // splits of a vocabulary row in a fixed order, so the result is deterministic.
 //
@@ -25,56 +30,60 @@
 namespace swvr {
 namespace tc {
 
-// KH: 64-wide K halves per pipeline stage (2 -> 8 MMAs per barrier round trip of the
-// single MMA-issuing thread); STG: dS^T goes out through a staged TMA store (else direct
-// 16-byte stores from registers, which frees the staging tile for a deeper pipeline).
-template <bool kBF16, int DP, int NS, int KH, bool STG>
+// KH: 64-wide K halves per pipeline stage (8 MMAs per barrier round trip of the single
+// MMA-issuing thread).
+template <bool kBF16, int DP, int NS, int KH>
 struct BwdCfg {
   static constexpr int BOX = 128 * 128;   // 128 rows x 128 bytes (64 16-bit elements)
   static constexpr int HBOX = 64 * 128;   // 64 rows x 128 bytes
   static constexpr int A_BYTES = KH * BOX;   // this CTA's 128 W rows x 64*KH K
   static constexpr int B_BYTES = KH * HBOX;  // this CTA's 64 h rows x 64*KH K
-  static constexpr int E_BYTES = (DP / 64) * BOX;     // this CTA's 128 E rows x DP
-  static constexpr int GOK_BYTES = (DP / 64) * HBOX;  // this CTA's 64 tokens x DP (K-major)
-  static constexpr int GOM_BYTES = BOX;               // 128 tokens x this CTA's 64 columns (MN-major)
+  static constexpr int DEN = DP == 64 ? 64 : 128;      // dE MMA N (embedding columns, padded)
+  static constexpr int GOM_W = DEN / 2;                // embedding columns of gO this CTA stages for dE
+  static constexpr int GOM_ROW = GOM_W * 2;            // bytes per token row of that copy (64 or 128)
+  static constexpr int GOM_BYTES = 128 * GOM_ROW;      // 128 tokens, MN-major
+  static constexpr int E_BYTES = (DP / 64) * BOX;      // this CTA's 128 E rows x DP
+  static constexpr int GOK_BYTES = (DP / 64) * HBOX;   // this CTA's 64 tokens x DP (K-major)
   static constexpr int SMEM_A = 0;
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
-  static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
-  static constexpr int SMEM_GOK = SMEM_E + E_BYTES;
-  static constexpr int SMEM_GOM = SMEM_GOK + 2 * GOK_BYTES;
-  static constexpr int SMEM_STG = SMEM_GOM + 2 * GOM_BYTES;  // dS tile staging: two 128 x 64 boxes
-  static constexpr int SMEM_LSE = SMEM_STG + (STG ? 2 * BOX : 0);
+  static constexpr int SMEM_GOM = SMEM_B + NS * B_BYTES;  // operand reads stay below SMEM_E
+  static constexpr int SMEM_GOK = SMEM_GOM + GOM_BYTES;
+  static constexpr int SMEM_E = SMEM_GOK + GOK_BYTES;
+  static constexpr int SMEM_LSE = SMEM_E + E_BYTES;
   static constexpr int SMEM_DELTA = SMEM_LSE + 512;
   static constexpr int SMEM_BAR = SMEM_DELTA + 512;
-  static constexpr int NBAR = 2 * NS + 13;
+  static constexpr int NBAR = 2 * NS + 14;
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
-  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;  // dE: 128 columns (N padded)
+  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;
+  static_assert(DE_COL + DEN <= 512, "TMEM budget");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
   static_assert(DP == 64 || DP == 128, "D padding");
+  static_assert(GOM_BYTES % 1024 == 0 && GOK_BYTES % 1024 == 0, "1024-byte alignment");
 };
 
-template <bool kBF16, int DP, int NS, int KH, bool STG>
+template <bool kBF16, int DP, int NS, int KH>
 __global__ void __launch_bounds__(256, 1)
     bwd_scores_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_h64,
-                      const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_go64,
-                      const __grid_constant__ CUtensorMap tm_go128, const __grid_constant__ CUtensorMap tm_ds,
-                      const BwdScoresParams p) {
-  using Cfg = BwdCfg<kBF16, DP, NS, KH, STG>;
+                      const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_gok,
+                      const __grid_constant__ CUtensorMap tm_gom, const BwdScoresParams p) {
+  using Cfg = BwdCfg<kBF16, DP, NS, KH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_BAR);
-  uint64_t* full = bars;              // [NS] leader: both CTAs' bytes
-  uint64_t* empty = bars + NS;        // [NS] both (multicast commit)
-  uint64_t* e_full = bars + 2 * NS;   // leader: both CTAs' bytes
-  uint64_t* e_empty = e_full + 1;     // both
-  uint64_t* go_full = e_empty + 1;    // [2] leader: both CTAs' bytes
-  uint64_t* go_empty = go_full + 2;   // [2] both
-  uint64_t* s_full = go_empty + 2;    // [2] both
-  uint64_t* dp_full = s_full + 2;     // both
-  uint64_t* p_ready = dp_full + 1;    // [2] leader: one arrival per CTA
-  uint64_t* de_full = p_ready + 2;    // both
-  uint64_t* de_free = de_full + 1;    // leader: one arrival per CTA
+  uint64_t* full = bars;               // [NS] leader: both CTAs' bytes
+  uint64_t* empty = bars + NS;         // [NS] both (multicast commit)
+  uint64_t* e_full = bars + 2 * NS;    // leader: both CTAs' bytes
+  uint64_t* e_empty = e_full + 1;      // both
+  uint64_t* gok_full = e_empty + 1;    // leader: both CTAs' bytes
+  uint64_t* gok_empty = gok_full + 1;  // both
+  uint64_t* gom_full = gok_empty + 1;  // leader: both CTAs' bytes
+  uint64_t* gom_empty = gom_full + 1;  // both
+  uint64_t* s_full = gom_empty + 1;    // [2] both
+  uint64_t* dp_full = s_full + 2;      // both
+  uint64_t* p_ready = dp_full + 1;     // [2] leader: one arrival per CTA
+  uint64_t* de_full = p_ready + 2;     // both
+  uint64_t* de_free = de_full + 1;     // leader: one arrival per CTA
   uint64_t* spare = de_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -93,9 +102,11 @@ __global__ void __launch_bounds__(256, 1)
     }
     mbar_init(e_full, 1);
     mbar_init(e_empty, 1);
+    mbar_init(gok_full, 1);
+    mbar_init(gok_empty, 1);
+    mbar_init(gom_full, 1);
+    mbar_init(gom_empty, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&go_full[b], 1);
-      mbar_init(&go_empty[b], 1);
       mbar_init(&s_full[b], 1);
       mbar_init(&p_ready[b], 2);
     }
@@ -110,9 +121,8 @@ __global__ void __launch_bounds__(256, 1)
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_h64);
     tma_prefetch_desc(&tm_e);
-    tma_prefetch_desc(&tm_go64);
-    tma_prefetch_desc(&tm_go128);
-    if (p.ds) tma_prefetch_desc(&tm_ds);
+    tma_prefetch_desc(&tm_gok);
+    tma_prefetch_desc(&tm_gom);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, 512);
@@ -124,23 +134,20 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
+  const int kx = min(NS, KB - 1);                  // stage after which a tile's E / gO loads are issued
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer (both CTAs)
+      // E, gO (K-major) of tile i and gO (MN-major) of tile i-1 are loaded after stage kx of
+      // tile i's W / h loads: by then the MMAs that last read those buffers have completed
+      // (in-order MMA execution), so the waits below do not stall the W / h stream.
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
       for (int u = pair; u < p.units; u += npairs) {
         const int vt = u / p.TS, ts = u % p.TS;
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         if (it1 <= it0) continue;
         const int vrow0 = p.v_begin + vt * 256 + static_cast<int>(rank) * 128;
-        if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
-        if (leader) mbar_arrive_expect_tx(e_full, 2 * Cfg::E_BYTES);
-        {
-          const uint32_t eb = mapa_shared(smem_u32(e_full), 0);
-#pragma unroll
-          for (int c = 0; c < DP / 64; ++c) tma_load_2d_pair(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, eb, c * 64, vrow0);
-        }
         for (int it = it0; it < it1; ++it, ++g) {
           const int trow = it * 128 + static_cast<int>(rank) * 64;
           for (int kb = 0; kb < KB; ++kb) {
@@ -157,17 +164,36 @@ __global__ void __launch_bounds__(256, 1)
               stage = 0;
               sphase ^= 1u;
             }
-          }
-          const uint32_t gb = g & 1u, use = g >> 1;
-          if (!mbar_wait(&go_empty[gb], (use & 1u) ^ 1u, abort_flag, kErrBwdScores | 3)) goto done;
-          if (leader) mbar_arrive_expect_tx(&go_full[gb], 2 * (Cfg::GOK_BYTES + Cfg::GOM_BYTES));
-          const uint32_t gob = mapa_shared(smem_u32(&go_full[gb]), 0);
+            if (kb != kx) continue;
+            if (it == it0) {
+              if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
+              if (leader) mbar_arrive_expect_tx(e_full, 2 * Cfg::E_BYTES);
+              const uint32_t eb = mapa_shared(smem_u32(e_full), 0);
 #pragma unroll
-          for (int c = 0; c < DP / 64; ++c)
-            tma_load_2d_pair(smem + Cfg::SMEM_GOK + gb * Cfg::GOK_BYTES + c * Cfg::HBOX, &tm_go64, gob, c * 64, trow);
-          tma_load_2d_pair(smem + Cfg::SMEM_GOM + gb * Cfg::GOM_BYTES, &tm_go128, gob, static_cast<int>(rank) * 64,
-                           it * 128);
+              for (int c = 0; c < DP / 64; ++c)
+                tma_load_2d_pair(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, eb, c * 64, vrow0);
+            }
+            if (!mbar_wait(gok_empty, (g & 1u) ^ 1u, abort_flag, kErrBwdScores | 3)) goto done;
+            if (leader) mbar_arrive_expect_tx(gok_full, 2 * Cfg::GOK_BYTES);
+            {
+              const uint32_t gb = mapa_shared(smem_u32(gok_full), 0);
+#pragma unroll
+              for (int c = 0; c < DP / 64; ++c)
+                tma_load_2d_pair(smem + Cfg::SMEM_GOK + c * Cfg::HBOX, &tm_gok, gb, c * 64, trow);
+            }
+            if (it > it0) {
+              if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+              if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+              tma_load_2d_pair(smem + Cfg::SMEM_GOM, &tm_gom, mapa_shared(smem_u32(gom_full), 0),
+                               static_cast<int>(rank) * Cfg::GOM_W, (it - 1) * 128);
+            }
+          }
         }
+        // the unit's last tile: its MN-major gO, once the previous tile's dE has read the buffer
+        if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+        if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+        tma_load_2d_pair(smem + Cfg::SMEM_GOM, &tm_gom, mapa_shared(smem_u32(gom_full), 0),
+                         static_cast<int>(rank) * Cfg::GOM_W, (it1 - 1) * 128);
         ++uc;
       }
     }
@@ -175,9 +201,11 @@ __global__ void __launch_bounds__(256, 1)
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer (leader only)
       const uint32_t idS = idesc_f16(kBF16, 256, 128, false, false);
-      const uint32_t idDE = idesc_f16(kBF16, 256, 128, false, true);
+      const uint32_t idDE = idesc_f16(kBF16, 256, Cfg::DEN, false, true);
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
       const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E);
+      const uint32_t gokbase = smem_u32(smem + Cfg::SMEM_GOK);
+      const uint32_t gombase = smem_u32(smem + Cfg::SMEM_GOM);
       // stage-0 descriptors; a stage / K half / 16-wide K step adds (byte offset >> 4)
       const uint64_t da0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);
       const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
@@ -186,8 +214,6 @@ __global__ void __launch_bounds__(256, 1)
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         const int n = it1 - it0;
         if (n <= 0) continue;
-        if (!mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 4)) goto done;
-        tc_fence_after();
         for (int j = 0; j <= n; ++j) {
           if (j < n) {
             const uint32_t b = g & 1u;
@@ -208,33 +234,37 @@ __global__ void __launch_bounds__(256, 1)
             umma2_commit_mc(&s_full[b], 3);
             // dP^T = E . dO^T into the single dP buffer: both CTAs' gradient passes of the
             // previous tile must have finished reading it.
+            if (j == 0 && !mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 6)) goto done;
             if (j > 0 && !mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 6))
               goto done;
-            if (!mbar_wait(&go_full[b], (g >> 1) & 1u, abort_flag, kErrBwdScores | 7)) goto done;
+            if (!mbar_wait(gok_full, g & 1u, abort_flag, kErrBwdScores | 7)) goto done;
             tc_fence_after();
-            const uint32_t gokbase = smem_u32(smem + Cfg::SMEM_GOK + b * Cfg::GOK_BYTES);
 #pragma unroll
             for (int ks = 0; ks < DP / 16; ++ks)
               umma2_ss(tmem + Cfg::DP_COL, sdesc_sw128(ebase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024),
                        sdesc_sw128(gokbase + (ks >> 2) * Cfg::HBOX + (ks & 3) * 32, 16, 1024), idS, ks ? 1u : 0u);
+            umma2_commit_mc(gok_empty, 3);
             umma2_commit_mc(dp_full, 3);
             ++g;
           }
           if (j > 0) {
             const uint32_t gg = g - 1u - (j < n ? 1u : 0u);
-            const uint32_t bb = gg & 1u;
-            if (j == n && !mbar_wait(&p_ready[bb], (gg >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+            if (j == n && !mbar_wait(&p_ready[gg & 1u], (gg >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+            if (!mbar_wait(gom_full, gg & 1u, abort_flag, kErrBwdScores | 9)) goto done;
             if (need_de) {
               const bool first = (j == 1);
               if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
               tc_fence_after();
-              const uint32_t gombase = smem_u32(smem + Cfg::SMEM_GOM + bb * Cfg::GOM_BYTES);
 #pragma unroll
-              for (int ks = 0; ks < 8; ++ks)
-                umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + bb * 128 + ks * 8,
-                         sdesc_sw128(gombase + ks * 2048, Cfg::BOX, 1024), idDE, (first && ks == 0) ? 0u : 1u);
+              for (int ks = 0; ks < 8; ++ks) {
+                const uint64_t bdesc = Cfg::GOM_ROW == 64
+                                           ? sdesc_sw64(gombase + ks * 16 * 64, Cfg::GOM_BYTES, 512)
+                                           : sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BYTES, 1024);
+                umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + (gg & 1u) * 128 + ks * 8, bdesc, idDE,
+                         (first && ks == 0) ? 0u : 1u);
+              }
             }
-            umma2_commit_mc(&go_empty[bb], 3);
+            umma2_commit_mc(gom_empty, 3);
           }
         }
         umma2_commit_mc(e_empty, 3);
@@ -245,11 +275,10 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // -------------------------------------------------------------- gradient warps (both CTAs)
     // lse_s holds -LSE*log2e and delta_s holds -delta for the current token tile, so each
-    // pair of tokens costs a handful of packed f32x2 ops.  dS*s goes to a 128B-swizzled
-    // staging tile that one thread stores with two TMA bulk copies per token tile.
+    // pair of tokens costs a handful of packed f32x2 ops.  Each thread stores its row of
+    // dS*s (128 tokens, 256 contiguous bytes) with 16-byte stores.
     const int r = threadIdx.x - 128;
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    uint8_t* stg = smem + Cfg::SMEM_STG;
     const float2 sc2v = make_float2(p.sc2, p.sc2), scalev = make_float2(p.scale, p.scale);
     const uint32_t p_ready_leader = mapa_shared(smem_u32(p_ready), 0);
     const uint32_t de_free_leader = mapa_shared(smem_u32(de_free), 0);
@@ -266,8 +295,6 @@ __global__ void __launch_bounds__(256, 1)
       float2 db = make_float2(0.f, 0.f);
       for (int it = it0; it < it1; ++it, ++g) {
         const int t0 = it * 128;
-        // the previous tile's dS store must have finished reading the staging tile
-        if (STG && need_ds && r == 0) tma_store_wait_read<0>();
         named_bar_sync(1, 128);
         {
           const int t = t0 + r;
@@ -307,16 +334,7 @@ __global__ void __launch_bounds__(256, 1)
               pk_p[i / 2] = pack2<kBF16>(pv.x, pv.y);
             }
           }
-          if (STG && need_ds) {
-            // tokens [32c, 32c + 32) of row r: box c/2, 16-byte chunks (c%2)*4 + q, 128B swizzle
-            uint8_t* row = stg + (c >> 1) * Cfg::BOX + r * 128;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int jj = (c & 1) * 4 + q;
-              *reinterpret_cast<uint4*>(row + ((jj ^ (r & 7)) << 4)) =
-                  make_uint4(pk_ds[4 * q], pk_ds[4 * q + 1], pk_ds[4 * q + 2], pk_ds[4 * q + 3]);
-            }
-          } else if (need_ds && vvalid) {
+          if (need_ds && vvalid) {
             // 64 contiguous bytes of row r: tokens [t0 + 32c, t0 + 32c + 32)
             uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.ds) +
                                                   static_cast<int64_t>(local_row0 + r) * p.ld_ds + t0 + c * 32);
@@ -326,17 +344,9 @@ __global__ void __launch_bounds__(256, 1)
           if (need_de) tmem_st16(sbase + c * 16, pk_p);
         }
         if (need_de) tmem_wait_st();
-        if (STG && need_ds) fence_proxy_async_smem();
         tc_fence_before();
         named_bar_sync(1, 128);
-        if (r == 0) {
-          if (STG && need_ds) {
-            tma_store_2d(&tm_ds, stg, t0, local_row0);
-            tma_store_2d(&tm_ds, stg + Cfg::BOX, t0 + 64, local_row0);
-            tma_store_commit();
-          }
-          mbar_arrive_cluster(p_ready_leader + b * 8);
-        }
+        if (r == 0) mbar_arrive_cluster(p_ready_leader + b * 8);
       }
       const int64_t slot = static_cast<int64_t>(u) * 256 + static_cast<int>(rank) * 128 + r;
       if (need_de) {
@@ -362,7 +372,6 @@ __global__ void __launch_bounds__(256, 1)
       if (need_db && vvalid) p.part_db[slot] = db.x + db.y;
       ++uc;
     }
-    if (STG && need_ds && r == 0) tma_store_wait_all<0>();
   }
 done:
   tc_fence_before();
@@ -375,10 +384,10 @@ done:
   }
 }
 
-template <bool kBF16, int DP, int NS, int KH, bool STG>
+template <bool kBF16, int DP, int NS, int KH>
 static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int max_pairs, cudaStream_t st) {
-  using Cfg = BwdCfg<kBF16, DP, NS, KH, STG>;
-  auto kern = bwd_scores_kernel<kBF16, DP, NS, KH, STG>;
+  using Cfg = BwdCfg<kBF16, DP, NS, KH>;
+  auto kern = bwd_scores_kernel<kBF16, DP, NS, KH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -399,16 +408,16 @@ static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm
   int pairs = std::min(std::min(clusters, max_pairs), prm.units);
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  return cudaLaunchKernelEx(&cfg, kern, m.w, m.h64, m.e, m.go64, m.go128, m.ds, prm);
+  return cudaLaunchKernelEx(&cfg, kern, m.w, m.h64, m.e, m.gok, m.gom, prm);
 }
+
+int bwd_gom_width(int DP) { return DP == 64 ? 32 : 64; }
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
                                      int max_pairs, cudaStream_t st) {
   if (DP == 64)
-    return bf16 ? launch_bwd<true, 64, 3, 2, false>(maps, prm, max_pairs, st)
-                : launch_bwd<false, 64, 3, 2, false>(maps, prm, max_pairs, st);
-  return bf16 ? launch_bwd<true, 128, 4, 1, true>(maps, prm, max_pairs, st)
-              : launch_bwd<false, 128, 4, 1, true>(maps, prm, max_pairs, st);
+    return bf16 ? launch_bwd<true, 64, 4, 2>(maps, prm, max_pairs, st) : launch_bwd<false, 64, 4, 2>(maps, prm, max_pairs, st);
+  return bf16 ? launch_bwd<true, 128, 3, 2>(maps, prm, max_pairs, st) : launch_bwd<false, 128, 3, 2>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc
