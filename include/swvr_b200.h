@@ -50,8 +50,10 @@ enum swvr_reduction { SWVR_REDUCE_NONE = 0, SWVR_REDUCE_SUM = 1, SWVR_REDUCE_MEA
  * One readout problem.  h, W and E share `compute_dtype`; rows may be padded (ld* is the
  * row stride in elements, the last dimension is contiguous).  On the tensor-core path the
  * base pointers must be 16-byte aligned and ld* * element size a multiple of 16 bytes.
- * `chunk` is the number of vocabulary rows whose score gradients the backward stages at a
- * time (the reference's chunk_size); the tensor-core path rounds it up to a multiple of 128.
+ * `chunk` is the reference's chunk_size, the knob that bounds the backward's working set:
+ * the reference stages chunk x N fp32 scores at a time; the tensor-core path stages its
+ * 16-bit score gradients for 2 * chunk vocabulary rows (rounded up to a multiple of 256),
+ * the same bytes, and the fp32 / fp64 path stages chunk rows.
  */
 typedef struct swvr_problem {
   int64_t n_tokens;   /* N  (rows of h)             */

@@ -289,8 +289,10 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   b.DP = p.embed_dim <= 64 ? 64 : 128;
   b.NT = static_cast<int>(ceil_div(p.n_tokens, 128));
   b.Npad = static_cast<int64_t>(b.NT) * 128;
-  // a multiple of 256 so that only the last chunk has a partial 256-row pair tile
-  int64_t C = round_up(std::max<int64_t>(p.chunk, 1), 256);
+  // The reference's chunk holds chunk x N fp32 scores; dS here is 16-bit, so the same bytes
+  // hold 2 * chunk rows.  A multiple of 256 so that only the last chunk has a partial
+  // 256-row pair tile.
+  int64_t C = round_up(2 * std::max<int64_t>(p.chunk, 1), 256);
   C = std::min<int64_t>(C, round_up(std::max<int64_t>(p.vocab, 1), 256));
   b.C = static_cast<int>(C);
   b.need_h = g.grad_h || g.grad_h_acc;
