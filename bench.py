@@ -57,6 +57,14 @@ def load_peaks():
         return 1590.0, 1400.0, "fallback"
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each tensor-core
+# kernel, from a one-pass ncu capture of one launch of this build at the named config on one
+# GPU with the default chunk (the full command is in the profiles/ summary of the DRAM traffic
+# at full size).  Other configs, chunk sizes or GPU counts report null.
+CAPTURED_TRAFFIC_GB = {("c2", "gemm_kernel"): 3.098, ("c2", "bwd_scores_kernel"): 1.730,
+                       ("c2", "fwd_kernel"): 10.530}
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 100 ms; ``summary`` keeps the samples
     taken between ``mark_start`` and ``mark_end`` (the timed region).  ``__enter__`` waits for the
@@ -383,7 +391,10 @@ def main():
             "peak_mem_gib": round(r["peak_gib"], 3),
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1) if achieved else None,
                          "peak": sustained, "unit": "TFLOP/s",
-                         "frac": round(achieved / sustained, 4) if achieved else None, "traffic": None,
+                         "frac": round(achieved / sustained, 4) if achieved else None,
+                         "traffic": (CAPTURED_TRAFFIC_GB.get((args.config, dom))
+                                     if world == 1 and args.chunk is None else None),
+                         "traffic_unit": "GB per launch (ncu dram read + write)",
                          "peak_kind": f"{peak_src} sustained cuBLAS bf16 (kernel timed inside a long step)"},
             "kernels": kernels,
             "gpu_launches": launches,

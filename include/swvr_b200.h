@@ -52,8 +52,9 @@ enum swvr_reduction { SWVR_REDUCE_NONE = 0, SWVR_REDUCE_SUM = 1, SWVR_REDUCE_MEA
  * base pointers must be 16-byte aligned and ld* * element size a multiple of 16 bytes.
  * `chunk` is the reference's chunk_size, the knob that bounds the backward's working set:
  * the reference stages chunk x N fp32 scores at a time; the tensor-core path stages its
- * 16-bit score gradients for 2 * chunk vocabulary rows (rounded up to a multiple of 256),
- * the same bytes, and the fp32 / fp64 path stages chunk rows.
+ * 16-bit score gradients for at most 2 * chunk vocabulary rows (the same bytes; the vocab
+ * is cut into equal chunks of a multiple of 256 rows), and the fp32 / fp64 path stages
+ * chunk rows.
  */
 typedef struct swvr_problem {
   int64_t n_tokens;   /* N  (rows of h)             */

@@ -292,8 +292,11 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   // The reference's chunk holds chunk x N fp32 scores; dS here is 16-bit, so the same bytes
   // hold 2 * chunk rows.  A multiple of 256 so that only the last chunk has a partial
   // 256-row pair tile.
-  int64_t C = round_up(2 * std::max<int64_t>(p.chunk, 1), 256);
-  C = std::min<int64_t>(C, round_up(std::max<int64_t>(p.vocab, 1), 256));
+  // The chunks are balanced: as many as that bound needs, of equal size, so no small tail
+  // chunk runs a mostly idle grid.
+  const int64_t cmax = round_up(2 * std::max<int64_t>(p.chunk, 1), 256);
+  const int64_t nch = ceil_div(std::max<int64_t>(p.vocab, 1), cmax);
+  int64_t C = round_up(ceil_div(std::max<int64_t>(p.vocab, 1), nch), 256);
   b.C = static_cast<int>(C);
   b.need_h = g.grad_h || g.grad_h_acc;
   b.need_W = g.grad_W != nullptr;
