@@ -38,6 +38,16 @@ def _tensor_core(cdt: torch.dtype) -> bool:
     return cdt in (torch.bfloat16, torch.float16)
 
 
+TC_MAX_D = 128  # widest embedding of the tensor-core kernels (O / dE accumulators in TMEM)
+
+
+def _engine_dtype(cdt: torch.dtype, D: int) -> torch.dtype:
+    """The dtype the library computes in.  bf16 / fp16 run the tensor-core kernels up to
+    D = 128; wider embeddings (the reference accepts any D) run the exact fp32 SIMT kernels on
+    fp32 copies of the operands, which is at least as accurate as the 16-bit contract."""
+    return torch.float32 if _tensor_core(cdt) and D > TC_MAX_D else cdt
+
+
 def _require_cuda(*tensors) -> torch.device:
     dev = tensors[0].device
     if dev.type != "cuda":
@@ -124,8 +134,9 @@ def _forward(h, W, E, bias, logit_scale, chunk, cdt):
         return O, lse
     if V == 0:  # the reference's loop never runs: O = 0 / 0, LSE = -inf + log(0)
         return O.fill_(float("nan")), lse.fill_(float("-inf"))
-    hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
-    p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
+    edt = _engine_dtype(cdt, D)
+    hc, Wc, Ec, b = _prepare(h, W, E, bias, edt)
+    p = _problem(hc, Wc, Ec, b, logit_scale, chunk, edt)
     lib = nat.lib()
     nbytes = nat.c_size_t(0)
     with torch.cuda.device(dev):
@@ -148,8 +159,9 @@ def _grad_buffer(x: torch.Tensor, cdt: torch.dtype, tc: bool) -> Tuple[torch.Ten
 def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b):
     dev = _require_cuda(h, W, E, bias, gO, glse, O, lse)
     adt = O.dtype
-    tc = _tensor_core(cdt)
     N, K, V, D = h.shape[0], h.shape[1], W.shape[0], E.shape[1]
+    cdt = _engine_dtype(cdt, D)
+    tc = _tensor_core(cdt)
     need_b = need_b and bias is not None
     gh = torch.empty(h.shape, dtype=h.dtype, device=dev) if need_h else None
     gW_buf, gW = _grad_buffer(W, cdt, tc) if need_W else (None, None)

@@ -92,9 +92,10 @@ def test_golden_bf16(name):
 # ------------------------------------------------------------------------------ test_cuda.py contracts
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("chunk", [1024, 3000])
-@pytest.mark.parametrize("D", [5, 16, 128])
+@pytest.mark.parametrize("D", [5, 16, 128, 200])
 def test_low_precision_matches_fp64(dtype, chunk, D):
-    """test_cuda.py:37-54 with the fp64 numpy oracle as the checker."""
+    """test_cuda.py:37-54 with the fp64 numpy oracle as the checker (D = 200 runs the fp32 SIMT
+    kernels: the tensor-core kernels stop at D = 128)."""
     N, K, V = 517, 512, 10007
     inputs = make_gpu(N, K, V, D, dtype)
     g = torch.Generator().manual_seed(3)
