@@ -10,8 +10,8 @@ forward   each rank runs the fused kernel over its shard and keeps the per-row s
           (``swvr_combine``), so O and LSE are bit-identical on all ranks.
 backward  every rank gets the same (dO, dLSE) because the loss is computed on the
           replicated O, LSE; it runs the fused backward over its shard (dW, dE, db are
-          local and final) and accumulates its partial dh in fp32; one all-reduce (SUM)
-          of dh [N, K] fp32 finishes dh.
+          local and final) and accumulates its partial dh in fp32; a reduce-scatter (SUM)
+          of dh [N, K] fp32 and an all-gather of the slabs cast to h's dtype finish dh.
 
 The compute backend is pluggable so the collective logic can be exercised on CPU ``gloo``
 ranks in tests; the default is libswvr_b200.so and nothing else runs in production.
@@ -123,6 +123,25 @@ def set_backend(backend) -> None:
     _BACKEND = backend if backend is not None else NativeBackend
 
 
+def _sum_dh_over_shards(dh: torch.Tensor, out_dtype: torch.dtype, group) -> torch.Tensor:
+    """The sum over ranks of the shards' dh partials, in ``out_dtype`` on every rank.
+
+    A reduce-scatter in the accumulation dtype (each rank sums one slab of rows, in a fixed
+    order) followed by an all-gather of the slabs already cast to h's dtype: the same fp32
+    sum as an all-reduce, with 3/4 of its traffic for a 16-bit h.  Every rank takes both
+    collectives exactly once per backward, frozen h or not."""
+    world = dist.get_world_size(group)
+    N, K = dh.shape
+    rows = -(-N // world)
+    if rows * world != N:
+        dh = torch.nn.functional.pad(dh, (0, 0, 0, rows * world - N))
+    slab = torch.empty(rows, K, dtype=dh.dtype, device=dh.device)
+    dist.reduce_scatter_tensor(slab, dh.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    full = torch.empty(rows * world, K, dtype=out_dtype, device=dh.device)
+    dist.all_gather_into_tensor(full, slab.to(out_dtype), group=group)
+    return full[:N]
+
+
 class _VocabParallelReadout(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, W, E, bias, scale, chunk, cdt, group):
@@ -148,9 +167,8 @@ class _VocabParallelReadout(torch.autograd.Function):
         need_h, need_W, need_E, need_b = ctx.needs_input_grad[:4]
         dh, gW, gE, gb = _BACKEND.backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_W, need_E,
                                            need_b and bias is not None)
-        # every rank reaches this collective exactly once per backward, frozen h or not
-        dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=group)
-        gh = dh.to(h.dtype) if need_h else None
+        gh = _sum_dh_over_shards(dh, h.dtype, group)
+        gh = gh if need_h else None
         return (gh, gW if need_W else None, gE if need_E else None, gb if need_b else None, None, None, None, None)
 
 

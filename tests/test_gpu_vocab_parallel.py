@@ -1,0 +1,95 @@
+"""Vocabulary-sharded readout on 2 GPUs over NCCL against the single-GPU path.
+
+Two ranks (spawned processes, one GPU each, NCCL with a short process-group timeout) own
+halves of W, E and b; their O, LSE, dh (the sum over shards) and shard gradients must match
+the single-GPU API on the full vocabulary.  The per-shard kernels are the same as on one GPU
+but the merge order differs (the softmax state of the shards is combined in rank order, dh
+is summed by a reduce-scatter), so the bound is the bf16 tolerance.  Skipped with fewer than
+two GPUs; the host logic of this path is covered on CPU gloo ranks
+(test_gloo_vocab_parallel.py).
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+N, K, V, D = 1000, 512, 30011, 64
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(5)
+    h = torch.randn(N, K, generator=g).to(torch.bfloat16)
+    W = (K ** -0.5 * torch.randn(V, K, generator=g)).to(torch.bfloat16)
+    E = (0.02 * torch.randn(V, D, generator=g)).to(torch.bfloat16)
+    b = (0.02 * torch.randn(V, generator=g)).to(torch.bfloat16)
+    t = 0.02 * torch.randn(N, D, generator=g)
+    w = (torch.rand(N, generator=g) < 0.9).float()
+    return h, W, E, b, t, w
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from swvr_b200 import vocab_parallel as vp
+    h, W, E, b, t, w = (x.cuda() for x in _inputs())
+    v0, v1 = vp.shard_range(V, world, rank)
+    hh = h.clone().requires_grad_(True)
+    Ws, Es, bs = (x[v0:v1].clone().requires_grad_(True) for x in (W, E, b))
+    loss = vp.softmax_readout_mse_vocab_parallel(hh, Ws, Es, t, bs, weight=w, z_loss_weight=1e-4, chunk_size=4096)
+    loss.backward()
+    O, lse = vp.softmax_readout_vocab_parallel(h, Ws.detach(), Es.detach(), bs.detach(), chunk_size=4096)
+    torch.cuda.synchronize()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), loss=loss.item(), O=O.float().cpu().numpy(),
+             lse=lse.float().cpu().numpy(), gh=hh.grad.float().cpu().numpy(), gW=Ws.grad.float().cpu().numpy(),
+             gE=Es.grad.float().cpu().numpy(), gb=bs.grad.float().cpu().numpy(), v0=v0, v1=v1)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_vocab_parallel_matches_single_gpu(tmp_path):
+    import swvr_b200 as swvr
+    from tests.helpers import rel_err
+
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+    h, W, E, b, t, w = (x.cuda() for x in _inputs())
+    hh, Wf, Ef, bf = (x.clone().requires_grad_(True) for x in (h, W, E, b))
+    loss = swvr.softmax_readout_mse(hh, Wf, Ef, t, bf, weight=w, z_loss_weight=1e-4, chunk_size=4096)
+    loss.backward()
+    O, lse = swvr.softmax_readout(h, W, E, b, chunk_size=4096)
+    for r in range(2):
+        z = np.load(os.path.join(str(tmp_path), f"rank{r}.npz"))
+        v0, v1 = int(z["v0"]), int(z["v1"])
+        assert abs(float(z["loss"]) - loss.item()) <= 1e-3 * abs(loss.item())
+        assert rel_err(torch.from_numpy(z["O"]), O) < 2e-2
+        assert np.max(np.abs(z["lse"] - lse.float().cpu().numpy())) < 1e-2
+        assert rel_err(torch.from_numpy(z["gh"]), hh.grad) < 2e-2
+        assert rel_err(torch.from_numpy(z["gW"]), Wf.grad[v0:v1]) < 2e-2
+        assert rel_err(torch.from_numpy(z["gE"]), Ef.grad[v0:v1]) < 2e-2
+        assert rel_err(torch.from_numpy(z["gb"]), bf.grad[v0:v1]) < 2e-2
