@@ -12,34 +12,55 @@ namespace small {
 // ------------------------------------------------------------------ combine
 // Source s of row n lives at idx(s, n): split slots of the tensor-core forward (mode 0,
 // T = tile_rows: ((n/T)*splits + s)*T + n%T) or shard-major arrays (mode 1: s*N + n).
+// One warp per row: the lanes split the sources for the max and the weights
+// w_s = 2^(m2_s - max) (exp2f for fp32 state), then split the D columns; the sums run in
+// double in source order for every column, and through a fixed shuffle tree for l, so the
+// result is deterministic and identical on every device that merges the same states.
+__device__ __forceinline__ float exp2_t(float x) { return exp2f(x); }
+__device__ __forceinline__ double exp2_t(double x) { return exp2(x); }
+
 template <typename T>
 __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict__ m2, const T* __restrict__ l,
                                const T* __restrict__ acc, int mode, int splits, int tile_rows, T* O, T* lse, T* m2o,
                                T* lo, T* acco) {
-  const int64_t n = blockIdx.x;
-  auto idx = [&](int s) -> int64_t {
-    return mode == 0 ? ((n / tile_rows) * splits + s) * tile_rows + (n % tile_rows) : static_cast<int64_t>(s) * N + n;
-  };
-  double M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmax(M, static_cast<double>(m2[idx(s)]));
-  const double ref = isinf(M) ? 0.0 : M;
-  double L = 0.0;
-  for (int s = 0; s < S; ++s) {
-    const double w = exp2(static_cast<double>(m2[idx(s)]) - ref);
-    L += w == 0.0 ? 0.0 : static_cast<double>(l[idx(s)]) * w;
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (n >= N) return;
+  // idx(s) = base + s * stride (integer divisions once per row, not per access)
+  const int64_t base = mode == 0 ? (n / tile_rows) * splits * tile_rows + n % tile_rows : n;
+  const int64_t stride = mode == 0 ? tile_rows : N;
+  auto idx = [&](int s) -> int64_t { return base + static_cast<int64_t>(s) * stride; };
+  T M = -INFINITY;
+  for (int s = lane; s < S; s += 32) M = fmax(M, m2[idx(s)]);
+  for (int o = 16; o > 0; o >>= 1) M = fmax(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const T ref = isinf(M) ? T(0) : M;
+  // weights of the first 64 sources stay in two registers per lane; more are recomputed
+  T w0 = 0, w1 = 0;
+  double Lp = 0.0;
+  for (int s = lane; s < S; s += 32) {
+    const T w = exp2_t(m2[idx(s)] - ref);
+    Lp += w == T(0) ? 0.0 : static_cast<double>(l[idx(s)]) * static_cast<double>(w);
+    if (s < 32) w0 = w;
+    else if (s < 64) w1 = w;
   }
-  for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int o = 16; o > 0; o >>= 1) Lp += __shfl_xor_sync(0xffffffffu, Lp, o);
+  const double L = Lp;
+  for (int64_t d0 = 0; d0 < D; d0 += 32) {  // uniform trip count: the shuffles below need every lane
+    const int64_t d = d0 + lane;
     double A = 0.0;
     for (int s = 0; s < S; ++s) {
-      const double w = exp2(static_cast<double>(m2[idx(s)]) - ref);
-      A += w == 0.0 ? 0.0 : static_cast<double>(acc[idx(s) * D + d]) * w;
+      const T ws = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
+      const T w = s < 64 ? ws : exp2_t(m2[idx(s)] - ref);
+      if (d < D && w != T(0)) A += static_cast<double>(acc[idx(s) * D + d]) * static_cast<double>(w);
     }
-    if (O) O[n * D + d] = static_cast<T>(A / L);
-    if (acco) acco[n * D + d] = static_cast<T>(A);
+    if (d < D) {
+      if (O) O[n * D + d] = static_cast<T>(A / L);
+      if (acco) acco[n * D + d] = static_cast<T>(A);
+    }
   }
-  if (threadIdx.x == 0) {
-    if (lse) lse[n] = static_cast<T>((ref + log2(L)) * 0.6931471805599453);
-    if (m2o) m2o[n] = static_cast<T>(M);
+  if (lane == 0) {
+    if (lse) lse[n] = static_cast<T>((static_cast<double>(ref) + log2(L)) * 0.6931471805599453);
+    if (m2o) m2o[n] = M;
     if (lo) lo[n] = static_cast<T>(L);
   }
 }
@@ -47,46 +68,50 @@ __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict_
 cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
                     int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st) {
   if (N == 0) return cudaSuccess;
-  const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
+  const unsigned blocks = static_cast<unsigned>(ceil_div(N, 8));  // 8 rows (warps) per block
   if (acc_dt == SWVR_F64)
-    combine_kernel<double><<<static_cast<unsigned>(N), threads, 0, st>>>(
+    combine_kernel<double><<<blocks, 256, 0, st>>>(
         S, N, D, static_cast<const double*>(m2), static_cast<const double*>(l), static_cast<const double*>(acc), mode,
         splits, tile_rows, static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
         static_cast<double*>(lo), static_cast<double*>(acco));
   else
-    combine_kernel<float><<<static_cast<unsigned>(N), threads, 0, st>>>(
+    combine_kernel<float><<<blocks, 256, 0, st>>>(
         S, N, D, static_cast<const float*>(m2), static_cast<const float*>(l), static_cast<const float*>(acc), mode,
-        splits, tile_rows, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o), static_cast<float*>(lo),
-        static_cast<float*>(acco));
+        splits, tile_rows, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o),
+        static_cast<float*>(lo), static_cast<float*>(acco));
   return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ dE / db reduction
-// Row v of the chunk: sum its TS token-split partial slots in split order.  Slots are
-// grouped per vocabulary tile of `tile_rows` rows: slot((vt*TS + ts)*tile_rows + r).
+// Row v of the chunk: sum its token-split partial slots in split order.  Slots are grouped
+// per vocabulary tile of `tile_rows` rows: slot((vt*TS + ts)*tile_rows + r), so for one
+// split the tile's rows x D floats are contiguous.  One thread per (row, column): the
+// loads of all splits are independent and go out together; the adds stay in split order.
 __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const float* __restrict__ part_db, int TS,
-                                    int per_t, int NT, int v_begin, int tile_rows, int64_t D, void* gE, int gE_dt,
+                                    int n_ts, int v_begin, int rows, int tile_rows, int64_t D, void* gE, int gE_dt,
                                     int64_t ld_gE, void* gb, int gb_dt) {
-  const int rr = blockIdx.x;  // row within the chunk
-  const int vt = rr / tile_rows, r = rr % tile_rows;
-  const int64_t v = v_begin + rr;
-  if (part_de) {
-    for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
-      float s = 0.f;
-      for (int ts = 0; ts < TS; ++ts) {
-        if (ts * per_t >= NT) break;
-        s += part_de[((static_cast<int64_t>(vt) * TS + ts) * tile_rows + r) * D + d];
-      }
-      store_f(gE, gE_dt, v * ld_gE + d, s);
-    }
-  }
-  if (part_db && threadIdx.x == 0) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (part_de && i < static_cast<int64_t>(rows) * D) {
+    const int64_t total = static_cast<int64_t>(rows) * D;
+    const int rr = total < (int64_t(1) << 32) ? static_cast<int>(static_cast<uint32_t>(i) / static_cast<uint32_t>(D))
+                                              : static_cast<int>(i / D);
+    const int64_t d = i - static_cast<int64_t>(rr) * D;
+    const int vt = rr / tile_rows, r = rr % tile_rows;
+    const float* src = part_de + (static_cast<int64_t>(vt) * TS * tile_rows + r) * D + d;
+    const int64_t step = static_cast<int64_t>(tile_rows) * D;
     float s = 0.f;
-    for (int ts = 0; ts < TS; ++ts) {
-      if (ts * per_t >= NT) break;
-      s += part_db[(static_cast<int64_t>(vt) * TS + ts) * tile_rows + r];
-    }
-    store_f(gb, gb_dt, v, s);
+#pragma unroll 4
+    for (int ts = 0; ts < n_ts; ++ts) s += src[ts * step];
+    store_f(gE, gE_dt, (v_begin + rr) * ld_gE + d, s);
+  }
+  if (part_db && i < rows) {
+    const int rr = static_cast<int>(i);
+    const int vt = rr / tile_rows, r = rr % tile_rows;
+    const float* src = part_db + static_cast<int64_t>(vt) * TS * tile_rows + r;
+    float s = 0.f;
+#pragma unroll 4
+    for (int ts = 0; ts < n_ts; ++ts) s += src[static_cast<int64_t>(ts) * tile_rows];
+    store_f(gb, gb_dt, v_begin + rr, s);
   }
 }
 
@@ -94,8 +119,10 @@ cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int
                          int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt,
                          cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  reduce_de_db_kernel<<<rows, D >= 128 ? 128 : 64, 0, st>>>(part_de, part_db, TS, per_t, NT, v_begin, tile_rows, D, gE,
-                                                             gE_dt, ld_gE, gb, gb_dt);
+  const int n_ts = std::min(TS, static_cast<int>(ceil_div(NT, std::max(per_t, 1))));  // splits with tokens
+  const int64_t work = std::max<int64_t>(part_de ? static_cast<int64_t>(rows) * D : 0, rows);
+  reduce_de_db_kernel<<<static_cast<unsigned>(ceil_div(work, 256)), 256, 0, st>>>(
+      part_de, part_db, TS, n_ts, v_begin, rows, tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
   return cudaGetLastError();
 }
 
