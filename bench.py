@@ -226,14 +226,22 @@ def run_ours(args, c, rank, world, device):
     t_dev = torch.empty_like(t)
     w_dev = torch.empty_like(w) if w is not None else None
     h2d = h_host.numel() * h_host.element_size() + t_host.numel() * 4 + (w_host.numel() * 4 if w is not None else 0)
+    if world > 1:  # each rank copies a 1/world row slab; NVLink all-gathers the rest
+        h2d = -(-h2d // world)
 
     def e2e_step():
-        h_dev.copy_(h_host, non_blocking=True)
-        t_dev.copy_(t_host, non_blocking=True)
-        if w_dev is not None:
-            w_dev.copy_(w_host, non_blocking=True)
-        hh = h_dev.detach().requires_grad_(True)
-        loss = step(hh, t_dev, w_dev)
+        if world > 1:
+            hd = vp.replicate_from_host(h_host, device)
+            td = vp.replicate_from_host(t_host, device)
+            wd = vp.replicate_from_host(w_host, device) if w_host is not None else None
+        else:
+            h_dev.copy_(h_host, non_blocking=True)
+            t_dev.copy_(t_host, non_blocking=True)
+            if w_dev is not None:
+                w_dev.copy_(w_host, non_blocking=True)
+            hd, td, wd = h_dev, t_dev, w_dev
+        hh = hd.detach().requires_grad_(True)
+        loss = step(hh, td, wd)
         loss_host.copy_(loss.detach(), non_blocking=True)
 
     for _ in range(2):
@@ -400,7 +408,10 @@ def main():
             "gpu_launches": launches,
             "clocks": r["clocks"],
             "e2e": {"value": round(F / (r["ms_e2e"] * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                    "ms_per_step": round(r["ms_e2e"], 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4},
+                    "ms_per_step": round(r["ms_e2e"], 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4,
+                    "h2d_scope": ("per rank: each rank copies 1/N of the replicated h, target and weight from pinned "
+                                  "host memory and NVLink all-gathers the rest (vocab_parallel.replicate_from_host)"
+                                  if world > 1 else "whole job")},
         }
         if world == 1 and not args.no_cpu_baseline:
             threads = cpu_threads()

@@ -204,6 +204,33 @@ def softmax_readout_mse_vocab_parallel(h, W_shard, E_shard, target, bias_shard=N
     return loss.view(lead) if reduction == "none" else loss
 
 
+def replicate_from_host(host: torch.Tensor, device=None, group=None, out: Optional[torch.Tensor] = None):
+    """A host tensor that every rank needs (h, target, weight), on this rank's device.
+
+    Each rank copies one slab of ceil(rows / G) rows from host memory (pinned, for an
+    asynchronous copy) and the slabs are all-gathered over NVLink, so each rank moves 1/G of
+    the tensor across PCIe instead of all of it.  Every rank must pass the same host data.
+    ``out`` (optional) is a device buffer of the full shape to gather into.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    device = torch.device(device) if device is not None else (out.device if out is not None else torch.device("cpu"))
+    rows = host.shape[0]
+    slab = -(-rows // world)
+    r0, r1 = min(rank * slab, rows), min((rank + 1) * slab, rows)
+    mine = torch.empty((slab, *host.shape[1:]), dtype=host.dtype, device=device)
+    if r1 > r0:
+        mine[:r1 - r0].copy_(host[r0:r1], non_blocking=True)
+    if r1 - r0 < slab:
+        mine[r1 - r0:].zero_()
+    full = torch.empty((slab * world, *host.shape[1:]), dtype=host.dtype, device=device)
+    dist.all_gather_into_tensor(full, mine, group=group)
+    if out is None:
+        return full[:rows]
+    out.copy_(full[:rows])
+    return out
+
+
 class VocabParallelSoftmaxReadoutMSE(nn.Module):
     """``SoftmaxReadoutMSE`` whose head / embedding rows are sharded over ``group``."""
 

@@ -132,3 +132,29 @@ def test_dead_rank_is_detected_by_timeout(tmp_path):
     assert procs[1].exitcode == 3
     status = (tmp_path / "rank0.txt").read_text()
     assert status.startswith("raised"), status
+
+
+def _replicate_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    from swvr_b200 import vocab_parallel as vp
+    g = torch.Generator().manual_seed(11)
+    host_h = torch.randn(7, 5, generator=g, dtype=torch.float64)   # 7 rows: not a multiple of world
+    host_w = torch.rand(7, generator=g)
+    got_h = vp.replicate_from_host(host_h)
+    buf = torch.full((7,), -1.0)
+    got_w = vp.replicate_from_host(host_w, out=buf)
+    np.savez(os.path.join(out_dir, f"rep{rank}.npz"), h=got_h.numpy(), w=got_w.numpy(), same=got_w is buf,
+             ref_h=host_h.numpy(), ref_w=host_w.numpy())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_replicate_from_host(tmp_path, world):
+    """Each rank copies a slab of the host tensor; the all-gather rebuilds it exactly everywhere."""
+    mp.spawn(_replicate_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        z = np.load(tmp_path / f"rep{r}.npz")
+        np.testing.assert_array_equal(z["h"], z["ref_h"])
+        np.testing.assert_array_equal(z["w"], z["ref_w"])
+        assert bool(z["same"])
