@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -98,7 +99,8 @@ class ClockSampler:
             self.gpu = str(device.index)
         self.proc = None
         self.t0 = self.t1 = None
-        self.out = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        log_dir = os.environ.get("SWVR_BENCH_LOG_DIR") or tempfile.gettempdir()
+        self.out = os.path.join(log_dir, f"clocks_bench_{os.getpid()}.csv")
 
     def __enter__(self):
         try:

@@ -1,6 +1,6 @@
 """Generate the golden vectors in this folder by running the reference library itself.
 
-    python tests/golden/make_golden.py [--ref /path/to/pengzhangzhi-swvr]
+    python tests/golden/make_golden.py --ref <reference checkout>   (or SWVR_REFERENCE=<checkout>)
 
 The reference (pengzhangzhi/swvr, pure Python on torch) is imported from ``--ref`` and run on
 CPU. Each case stores its seeded inputs and the reference's outputs and gradients as a
@@ -77,8 +77,11 @@ def case_f64(swvr, name, h, W, E, b, scale, chunk):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SWVR_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SWVR_REFERENCE"),
+                    help="checkout of the reference project (the directory holding swvr/); or SWVR_REFERENCE")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref <reference checkout> or set SWVR_REFERENCE")
     sys.path.insert(0, args.ref)
     import swvr  # the reference library
     torch.manual_seed(0)
