@@ -227,7 +227,7 @@ def run_ours(args, c, rank, world, device):
     # ---------------------------------------------------------------- device-resident timing
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device) as clocks, _native.profile() as prof:
+    with ClockSampler(device) as clocks:
         barrier()
         clocks.mark_start()
         ev0.record(stream)
@@ -238,6 +238,17 @@ def run_ours(args, c, rank, world, device):
         clocks.mark_end()
     ms = ev0.elapsed_time(ev1) / args.steps
     peak_gib = (torch.cuda.max_memory_allocated(device) - base) / 2 ** 30
+    _native.check_device_error()
+
+    # per-kernel breakdown: the same steps again under the library's launch accounting, which
+    # brackets every launch with CUDA events on its stream (kept out of the timed loop above:
+    # an event between two launches would also stop a kernel from starting while its
+    # predecessor drains)
+    barrier()
+    with _native.profile() as prof:
+        for _ in range(args.steps):
+            step(h, t, w)
+        barrier()
     _native.check_device_error()
 
     # ---------------------------------------------------------------- end to end (host buffers)

@@ -255,7 +255,7 @@ static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo
   SWVR_TRY(tc_fwd_launch(p, f, static_cast<char*>(ws), st, &prm));
   ProfScope ps_c(kProfCombine, st);
   SWVR_CUDA(small::combine(SWVR_F32, f.splits, p.n_tokens, p.embed_dim, prm.part_m2, prm.part_l, prm.part_acc, 0,
-                           f.splits, tc::kFwdTokenTile, O, lse, m2o, lo, acco, st));
+                           f.splits, tc::kFwdTokenTile, O, lse, m2o, lo, acco, /*pdl=*/true, st));
   return SWVR_OK;
 }
 
@@ -420,13 +420,14 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     }
     {
       ProfScope ps(kProfBwdScores, st);
-      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, b.sms / 2, st));
+      // after the first chunk the previous kernel in the stream is this loop's own
+      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
     }
     if (part_de || part_db) {
       void* gE = g.grad_E;
       ProfScope ps(kProfReduce, st);
       SWVR_CUDA(small::reduce_de_db(part_de, part_db, TS, per_t, b.NT, static_cast<int>(v0), rows, 256, D, gE,
-                                    g.grad_E_dtype, g.ld_grad_E, g.grad_bias, g.grad_bias_dtype, st));
+                                    g.grad_E_dtype, g.ld_grad_E, g.grad_bias, g.grad_bias_dtype, /*pdl=*/true, st));
     }
     if (b.need_ds) {
       tc::GemmParams gp{};
@@ -444,7 +445,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
       const int tiles = gp.dw_tiles + gp.dh_tiles;
       if (tiles > 0) {
         ProfScope ps(kProfGemm, st);
-        SWVR_CUDA(tc::launch_gemm_kernel(bf16, gm, gp, b.sms / 2, st));
+        SWVR_CUDA(tc::launch_gemm_kernel(bf16, gm, gp, b.sms / 2, /*pdl=*/true, st));
       }
     }
   }
@@ -552,7 +553,7 @@ int swvr_combine(int64_t shards, int64_t n_tokens, int64_t embed_dim, int32_t ac
   if (n_tokens > 0 && (!m2 || !l || !acc || !O || !lse)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
   ProfScope ps(kProfCombine, static_cast<cudaStream_t>(stream));
   SWVR_CUDA(small::combine(acc_dt, static_cast<int>(shards), n_tokens, embed_dim, m2, l, acc, 1, 1, 0, O, lse, nullptr,
-                           nullptr, nullptr, static_cast<cudaStream_t>(stream)));
+                           nullptr, nullptr, /*pdl=*/false, static_cast<cudaStream_t>(stream)));
   return SWVR_OK;
 }
 

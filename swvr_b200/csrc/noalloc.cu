@@ -93,6 +93,6 @@ extern "C" int swvr_fwd_noalloc(const swvr_problem* p, void* O, void* lse, void*
   SWVR_TRY(tc_fwd_launch(*p, f, static_cast<char*>(scratch), st, &prm));
   ProfScope ps_c(kProfCombine, st);
   SWVR_CUDA(small::combine(SWVR_F32, f.splits, p->n_tokens, p->embed_dim, prm.part_m2, prm.part_l, prm.part_acc, 0,
-                           f.splits, tc::kFwdTokenTile, O, lse, nullptr, nullptr, nullptr, st));
+                           f.splits, tc::kFwdTokenTile, O, lse, nullptr, nullptr, nullptr, /*pdl=*/true, st));
   return SWVR_OK;
 }

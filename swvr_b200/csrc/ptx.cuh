@@ -35,6 +35,15 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while its predecessor
+// in the stream is still running: pdl_wait() blocks until the predecessor grid has completed
+// and its memory is visible (call it before touching anything the predecessor writes or
+// reads), pdl_trigger() lets the successor's CTAs launch as SMs free up.  Both are no-ops
+// for a grid launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

@@ -4,10 +4,27 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "ptx.cuh"
 #include "small.cuh"
 
 namespace swvr {
 namespace small {
+
+// Launch a grid of plain blocks, optionally with programmatic stream serialization.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_small(void (*kern)(KArgs...), unsigned blocks, unsigned threads, bool pdl, cudaStream_t st,
+                                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.stream = st;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 // ------------------------------------------------------------------ combine
 // Source s of row n lives at idx(s, n): split slots of the tensor-core forward (mode 0,
@@ -23,6 +40,7 @@ template <typename T>
 __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict__ m2, const T* __restrict__ l,
                                const T* __restrict__ acc, int mode, int splits, int tile_rows, T* O, T* lse, T* m2o,
                                T* lo, T* acco) {
+  pdl_wait();
   const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (n >= N) return;
@@ -66,20 +84,19 @@ __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict_
 }
 
 cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
-                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st) {
+                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, bool pdl,
+                    cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   const unsigned blocks = static_cast<unsigned>(ceil_div(N, 8));  // 8 rows (warps) per block
   if (acc_dt == SWVR_F64)
-    combine_kernel<double><<<blocks, 256, 0, st>>>(
-        S, N, D, static_cast<const double*>(m2), static_cast<const double*>(l), static_cast<const double*>(acc), mode,
-        splits, tile_rows, static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
-        static_cast<double*>(lo), static_cast<double*>(acco));
-  else
-    combine_kernel<float><<<blocks, 256, 0, st>>>(
-        S, N, D, static_cast<const float*>(m2), static_cast<const float*>(l), static_cast<const float*>(acc), mode,
-        splits, tile_rows, static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o),
-        static_cast<float*>(lo), static_cast<float*>(acco));
-  return cudaGetLastError();
+    return launch_small(combine_kernel<double>, blocks, 256, pdl, st, S, N, D, static_cast<const double*>(m2),
+                        static_cast<const double*>(l), static_cast<const double*>(acc), mode, splits, tile_rows,
+                        static_cast<double*>(O), static_cast<double*>(lse), static_cast<double*>(m2o),
+                        static_cast<double*>(lo), static_cast<double*>(acco));
+  return launch_small(combine_kernel<float>, blocks, 256, pdl, st, S, N, D, static_cast<const float*>(m2),
+                      static_cast<const float*>(l), static_cast<const float*>(acc), mode, splits, tile_rows,
+                      static_cast<float*>(O), static_cast<float*>(lse), static_cast<float*>(m2o),
+                      static_cast<float*>(lo), static_cast<float*>(acco));
 }
 
 // ------------------------------------------------------------------ dE / db reduction
@@ -90,6 +107,7 @@ cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, con
 __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const float* __restrict__ part_db, int TS,
                                     int n_ts, int v_begin, int rows, int tile_rows, int64_t D, void* gE, int gE_dt,
                                     int64_t ld_gE, void* gb, int gb_dt) {
+  pdl_wait();
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (part_de && i < static_cast<int64_t>(rows) * D) {
     const int64_t total = static_cast<int64_t>(rows) * D;
@@ -116,14 +134,13 @@ __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const flo
 }
 
 cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
-                         int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt,
+                         int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt, bool pdl,
                          cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const int n_ts = std::min(TS, static_cast<int>(ceil_div(NT, std::max(per_t, 1))));  // splits with tokens
   const int64_t work = std::max<int64_t>(part_de ? static_cast<int64_t>(rows) * D : 0, rows);
-  reduce_de_db_kernel<<<static_cast<unsigned>(ceil_div(work, 256)), 256, 0, st>>>(
-      part_de, part_db, TS, n_ts, v_begin, rows, tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
-  return cudaGetLastError();
+  return launch_small(reduce_de_db_kernel, static_cast<unsigned>(ceil_div(work, 256)), 256, pdl, st, part_de, part_db,
+                      TS, n_ts, v_begin, rows, tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
 }
 
 // ------------------------------------------------------------------ backward prologue

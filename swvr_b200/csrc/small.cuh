@@ -4,10 +4,13 @@
 
 namespace swvr {
 namespace small {
+// pdl: launch with programmatic stream serialization (the previous kernel in the stream is
+// the one producing this kernel's input; the kernel waits for it before reading).
 cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, const void* l, const void* acc, int mode,
-                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, cudaStream_t st);
+                    int splits, int tile_rows, void* O, void* lse, void* m2o, void* lo, void* acco, bool pdl,
+                    cudaStream_t st);
 cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
-                         int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt,
+                         int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt, bool pdl,
                          cudaStream_t st);
 cudaError_t prologue(bool bf16, const float* O, const float* gO, const float* glse, int64_t N, int D, int DP,
                      float* delta, void* gOc, cudaStream_t st);

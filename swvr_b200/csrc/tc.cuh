@@ -62,8 +62,10 @@ struct BwdScoresMaps {
 int bwd_gom_width(int DP);
 
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
+// pdl: launch with programmatic stream serialization (the previous kernel in the stream is
+// one of ours whose reads of dS / the partial slots this kernel's stores wait for).
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                     int max_pairs, cudaStream_t st);
+                                     int max_pairs, bool pdl, cudaStream_t st);
 
 // ------------------------------------------------------------------ backward: dW / dh GEMMs
 struct GemmParams {
@@ -84,7 +86,7 @@ struct GemmMaps {
 };
 
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
-cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs,
+cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs, bool pdl,
                                cudaStream_t st);
 
 }  // namespace tc

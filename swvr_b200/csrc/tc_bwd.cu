@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(256, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  if (threadIdx.x == 0) pdl_trigger();
   const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
   const int kx = min(NS, KB - 1);                  // stage after which a tile's E / gO loads are issued
 
@@ -282,6 +283,9 @@ __global__ void __launch_bounds__(256, 1)
     const float2 sc2v = make_float2(p.sc2, p.sc2), scalev = make_float2(p.scale, p.scale);
     const uint32_t p_ready_leader = mapa_shared(smem_u32(p_ready), 0);
     const uint32_t de_free_leader = mapa_shared(smem_u32(de_free), 0);
+    // The loads and MMAs above read inputs only; the dS buffer and the partial slots written
+    // here are still read by the previous chunk's kernels until they complete.
+    pdl_wait();
     uint32_t g = 0, uc = 0;
     for (int u = pair; u < p.units; u += npairs) {
       const int vt = u / p.TS, ts = u % p.TS;
@@ -385,13 +389,14 @@ done:
 }
 
 template <bool kBF16, int DP, int NS, int KH>
-static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int max_pairs, cudaStream_t st) {
+static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm, int max_pairs, bool pdl,
+                              cudaStream_t st) {
   using Cfg = BwdCfg<kBF16, DP, NS, KH>;
   auto kern = bwd_scores_kernel<kBF16, DP, NS, KH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -408,16 +413,23 @@ static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm
   int pairs = std::min(std::min(clusters, max_pairs), prm.units);
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  if (pdl) {  // may start while the previous kernel in the stream drains (see pdl_wait in the kernel)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kern, m.w, m.h64, m.e, m.gok, m.gom, prm);
 }
 
 int bwd_gom_width(int DP) { return DP == 64 ? 32 : 64; }
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                     int max_pairs, cudaStream_t st) {
+                                     int max_pairs, bool pdl, cudaStream_t st) {
   if (DP == 64)
-    return bf16 ? launch_bwd<true, 64, 4, 2>(maps, prm, max_pairs, st) : launch_bwd<false, 64, 4, 2>(maps, prm, max_pairs, st);
-  return bf16 ? launch_bwd<true, 128, 3, 2>(maps, prm, max_pairs, st) : launch_bwd<false, 128, 3, 2>(maps, prm, max_pairs, st);
+    return bf16 ? launch_bwd<true, 64, 4, 2>(maps, prm, max_pairs, pdl, st)
+                : launch_bwd<false, 64, 4, 2>(maps, prm, max_pairs, pdl, st);
+  return bf16 ? launch_bwd<true, 128, 3, 2>(maps, prm, max_pairs, pdl, st)
+              : launch_bwd<false, 128, 3, 2>(maps, prm, max_pairs, pdl, st);
 }
 
 }  // namespace tc

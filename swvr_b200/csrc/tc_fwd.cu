@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(256, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  if (threadIdx.x == 0) pdl_trigger();  // the combine may launch early; it waits for this grid
   const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
 
   if (warp == 0) {

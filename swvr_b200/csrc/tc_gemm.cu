@@ -129,10 +129,12 @@ __global__ void __launch_bounds__(256, 1)
   cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  if (threadIdx.x == 0) pdl_trigger();  // the next chunk's score kernel may take SMs as they free up
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer (both CTAs)
+      pdl_wait();  // dS of this chunk comes from the kernels before this one
       uint32_t stage = 0, sphase = 0;
       for (int t = pair; t < ntiles; t += npairs) {
         const TileInfo ti = decode_tile(p, t);
@@ -267,13 +269,13 @@ done:
 }
 
 template <bool kBF16, int NS>
-static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pairs, cudaStream_t st) {
+static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pairs, bool pdl, cudaStream_t st) {
   using Cfg = GemmCfg<NS>;
   auto kern = gemm_kernel<kBF16, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -291,6 +293,11 @@ static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pair
   int pairs = std::min(std::min(clusters, max_pairs), tiles);
   if (pairs < 1) pairs = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  if (pdl) {  // may start while the previous kernel in the stream drains (see pdl_wait in the kernel)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   static bool reported = false;
   if (!reported && getenv("SWVR_DEBUG")) {
     fprintf(stderr, "[swvr] gemm_kernel: %d co-resident 2-CTA clusters, launching %d pairs for %d tiles\n", clusters,
@@ -300,9 +307,9 @@ static cudaError_t launch(const GemmMaps& m, const GemmParams& prm, int max_pair
   return cudaLaunchKernelEx(&cfg, kern, m.ds_k, m.ds_mn, m.h_mn, m.w_mn, m.gw, m.dh, prm);
 }
 
-cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs,
+cudaError_t launch_gemm_kernel(bool bf16, const GemmMaps& maps, const GemmParams& prm, int max_pairs, bool pdl,
                                cudaStream_t st) {
-  return bf16 ? launch<true, 3>(maps, prm, max_pairs, st) : launch<false, 3>(maps, prm, max_pairs, st);
+  return bf16 ? launch<true, 3>(maps, prm, max_pairs, pdl, st) : launch<false, 3>(maps, prm, max_pairs, pdl, st);
 }
 
 }  // namespace tc
