@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define SWVR_ABI_VERSION 1
+#define SWVR_ABI_VERSION 2
 
 enum swvr_status {
   SWVR_OK = 0,
@@ -124,7 +124,9 @@ int swvr_combine(int64_t shards, int64_t n_tokens, int64_t embed_dim, int32_t ac
  * inputs skip their GEMMs.  grad_W / grad_E rows may be padded (ld_* in elements).
  * grad_h_acc, when not NULL, is an fp32 (fp64 for F64 compute) [N, K] buffer that receives
  * the un-cast dh accumulator (a vocabulary shard's partial dh, summed across shards by the
- * caller); grad_h may then be NULL.
+ * caller); grad_h may then be NULL.  With accumulate_grad_h non-zero the backward adds into
+ * grad_h_acc instead of overwriting it, so a caller can run the vocabulary in pieces (for
+ * example to cast fp32 parameters to the compute dtype one piece at a time).
  */
 typedef struct swvr_grads {
   const void* grad_O;
@@ -142,6 +144,7 @@ typedef struct swvr_grads {
   void* grad_bias;
   int32_t grad_bias_dtype;
   void* grad_h_acc;
+  int32_t accumulate_grad_h;
 } swvr_grads;
 
 /*

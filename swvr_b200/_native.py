@@ -46,7 +46,7 @@ class Grads(ctypes.Structure):
         ("grad_W", c_void_p), ("grad_W_dtype", c_int32), ("ld_grad_W", c_int64),
         ("grad_E", c_void_p), ("grad_E_dtype", c_int32), ("ld_grad_E", c_int64),
         ("grad_bias", c_void_p), ("grad_bias_dtype", c_int32),
-        ("grad_h_acc", c_void_p),
+        ("grad_h_acc", c_void_p), ("accumulate_grad_h", c_int32),
     ]
 
 

@@ -342,7 +342,8 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     if (g.grad_E) SWVR_CUDA(small::zero_rows(g.grad_E, g.grad_E_dtype, V, D, g.ld_grad_E, st));
     if (g.grad_bias) SWVR_CUDA(small::zero_rows(g.grad_bias, g.grad_bias_dtype, 1, V, V, st));
     if (g.grad_h) SWVR_CUDA(small::zero_rows(g.grad_h, g.grad_h_dtype, N, K, K, st));
-    if (g.grad_h_acc) SWVR_CUDA(cudaMemsetAsync(g.grad_h_acc, 0, static_cast<size_t>(N) * K * 4, st));
+    if (g.grad_h_acc && !g.accumulate_grad_h)
+      SWVR_CUDA(cudaMemsetAsync(g.grad_h_acc, 0, static_cast<size_t>(N) * K * 4, st));
     return SWVR_OK;
   }
   const bool bf16 = p.compute_dtype == SWVR_BF16;
@@ -360,7 +361,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
   SWVR_CUDA(small::prologue(bf16, static_cast<const float*>(g.O), static_cast<const float*>(g.grad_O),
                             static_cast<const float*>(g.grad_lse), N, static_cast<int>(D), b.DP, delta, goc, st));
   }
-  if (dh) SWVR_CUDA(cudaMemsetAsync(dh, 0, static_cast<size_t>(N) * K * 4, st));
+  if (dh && !(g.grad_h_acc && g.accumulate_grad_h)) SWVR_CUDA(cudaMemsetAsync(dh, 0, static_cast<size_t>(N) * K * 4, st));
 
   tc::BwdScoresMaps sm;
   SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));

@@ -325,7 +325,7 @@ static int bwd_impl(const swvr_problem& p, const swvr_grads& g, void* ws, cudaSt
   }
   delta_kernel<T><<<grid_for(N), 256, 0, st>>>(static_cast<const T*>(g.O), gO, static_cast<const T*>(g.grad_lse), delta,
                                                N, D);
-  if (need_h) cudaMemsetAsync(dh, 0, sizeof(T) * N * K, st);
+  if (need_h && !(g.grad_h_acc && g.accumulate_grad_h)) cudaMemsetAsync(dh, 0, sizeof(T) * N * K, st);
   for (int64_t v0 = 0; v0 < V; v0 += C) {
     const int64_t c = (V - v0) < C ? (V - v0) : C;
     // P = exp(s h W_c^T + b_c - lse)  (chunked.py:132)

@@ -91,6 +91,8 @@ def _ld(x: torch.Tensor) -> int:
 
 
 def _problem(h, W, E, bias, scale, chunk, cdt) -> nat.Problem:
+    """The C struct for one call.  It holds raw device pointers only: the caller keeps h, W, E
+    and bias referenced until the launch that uses it has been issued."""
     p = nat.Problem()
     p.n_tokens, p.hidden = h.shape[0], h.shape[1]
     p.vocab, p.embed_dim = W.shape[0], E.shape[1]
@@ -105,19 +107,31 @@ def _problem(h, W, E, bias, scale, chunk, cdt) -> nat.Problem:
     return p
 
 
-def _prepare(h, W, E, bias, cdt):
-    """Operands as the library takes them.  K is zero-padded to a multiple of 8 on the
-    tensor-core path (zero columns add nothing to h . W^T)."""
-    K = h.shape[1]
+def _prepare_k(x, cdt):
+    """``x`` [rows, K] as the library takes it: in ``cdt``, with K zero-padded to a multiple of 8 on
+    the tensor-core path (zero columns add nothing to h . W^T)."""
+    K = x.shape[1]
     if _tensor_core(cdt) and K % 8 != 0:
-        K8 = (K + 7) // 8 * 8
-        h = torch.nn.functional.pad(h.to(cdt), (0, K8 - K))
-        W = torch.nn.functional.pad(W.to(cdt), (0, K8 - K))
-    hc = _operand(h, cdt)
-    Wc = _operand(W, cdt)
-    Ec = _operand(E, cdt)
+        x = torch.nn.functional.pad(x.to(cdt), (0, (K + 7) // 8 * 8 - K))
+    return _operand(x, cdt)
+
+
+def _prepare(h, W, E, bias, cdt):
+    """Operands as the library takes them (see ``_prepare_k``)."""
     b = bias.contiguous() if bias is not None else None
-    return hc, Wc, Ec, b
+    return _prepare_k(h, cdt), _prepare_k(W, cdt), _operand(E, cdt), b
+
+
+def _param_cast_chunks(W, E, cdt) -> bool:
+    """16-bit compute with parameters in another dtype (autocast over fp32 parameters): W and E
+    are cast one vocabulary chunk at a time, as the reference's ``W[v0:v1].to(cdt)``
+    (swvr/chunked.py:90-95, 120-146), not as whole copies."""
+    return _tensor_core(cdt) and (W.dtype != cdt or E.dtype != cdt)
+
+
+def _chunk_rows(V: int, chunk: int):
+    rows = max(int(chunk), 1)
+    return [(v0, min(v0 + rows, V)) for v0 in range(0, V, rows)]
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor:
@@ -135,6 +149,8 @@ def _forward(h, W, E, bias, logit_scale, chunk, cdt):
     if V == 0:  # the reference's loop never runs: O = 0 / 0, LSE = -inf + log(0)
         return O.fill_(float("nan")), lse.fill_(float("-inf"))
     edt = _engine_dtype(cdt, D)
+    if _param_cast_chunks(W, E, edt):
+        return _forward_param_cast(h, W, E, bias, logit_scale, chunk, edt, O, lse, dev)
     hc, Wc, Ec, b = _prepare(h, W, E, bias, edt)
     p = _problem(hc, Wc, Ec, b, logit_scale, chunk, edt)
     lib = nat.lib()
@@ -144,6 +160,34 @@ def _forward(h, W, E, bias, logit_scale, chunk, cdt):
         ws = _workspace(nbytes.value, dev)
         nat.check(lib.swvr_fwd(p, O.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
                   "swvr_fwd")
+    return O, lse
+
+
+def _forward_param_cast(h, W, E, bias, logit_scale, chunk, cdt, O, lse, dev):
+    """The forward over vocabulary chunks whose W / E rows are cast to ``cdt`` one chunk at a
+    time: each chunk's online-softmax state comes from ``swvr_fwd_partial`` and
+    ``swvr_combine`` merges them in chunk order."""
+    N, D = h.shape[0], E.shape[1]
+    spans = _chunk_rows(W.shape[0], chunk)
+    m2 = torch.empty(len(spans), N, dtype=O.dtype, device=dev)
+    l = torch.empty(len(spans), N, dtype=O.dtype, device=dev)
+    acc = torch.empty(len(spans), N, D, dtype=O.dtype, device=dev)
+    hc = _prepare_k(h, cdt)
+    lib = nat.lib()
+    with torch.cuda.device(dev):
+        for i, (v0, v1) in enumerate(spans):
+            # the problem holds raw pointers: the cast chunks must stay referenced until the
+            # launch, or the caching allocator may hand their memory to the workspace below
+            Wc, Ec = _prepare_k(W[v0:v1], cdt), _operand(E[v0:v1], cdt)
+            b = bias[v0:v1].contiguous() if bias is not None else None
+            p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
+            nbytes = nat.c_size_t(0)
+            nat.check(lib.swvr_fwd_workspace_size(p, nat.ctypes.byref(nbytes)), "swvr_fwd_workspace_size")
+            ws = _workspace(nbytes.value, dev)
+            nat.check(lib.swvr_fwd_partial(p, m2[i].data_ptr(), l[i].data_ptr(), acc[i].data_ptr(), ws.data_ptr(),
+                                           ws.numel(), nat.stream_ptr(dev)), "swvr_fwd_partial")
+        nat.check(lib.swvr_combine(len(spans), N, D, nat.dtype_code(O.dtype), m2.data_ptr(), l.data_ptr(),
+                                   acc.data_ptr(), O.data_ptr(), lse.data_ptr(), nat.stream_ptr(dev)), "swvr_combine")
     return O, lse
 
 
@@ -173,6 +217,9 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
         if gh is not None:
             gh.zero_()
         return gh, gW, gE, gb
+    if _param_cast_chunks(W, E, cdt):
+        return _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb,
+                                    dev)
     hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
     K8 = hc.shape[1]
     padded_k = K8 != K
@@ -203,6 +250,45 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
     if need_h and gh_buf is not gh:
         gh.copy_(gh_buf[:, :K])
     if need_W and gW_buf is not gW:
+        gW.copy_(gW_buf[:, :K])
+    return gh, gW, gE, gb
+
+
+def _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb, dev):
+    """The backward over vocabulary chunks whose W / E rows are cast to ``cdt`` one chunk at a
+    time: one ``swvr_bwd`` per chunk writes that chunk's rows of dW, dE, db and adds its dh
+    into one fp32 accumulator (``accumulate_grad_h``), which is cast once at the end."""
+    N, K = h.shape
+    hc = _prepare_k(h, cdt)
+    K8 = hc.shape[1]
+    dh = torch.empty(N, K8, dtype=torch.float32, device=dev) if gh is not None else None
+    if gW_buf is not None and K8 != K:
+        gW_buf = torch.empty(W.shape[0], K8, dtype=gW_buf.dtype, device=dev)
+    gO = gO.to(O.dtype).contiguous()
+    glse = glse.to(O.dtype).contiguous()
+    lib = nat.lib()
+    with torch.cuda.device(dev):
+        for i, (v0, v1) in enumerate(_chunk_rows(W.shape[0], chunk)):
+            Wc, Ec = _prepare_k(W[v0:v1], cdt), _operand(E[v0:v1], cdt)  # referenced until the launch
+            b = bias[v0:v1].contiguous() if bias is not None else None
+            p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
+            g = nat.Grads()
+            g.grad_O, g.grad_lse, g.O, g.lse = gO.data_ptr(), glse.data_ptr(), O.data_ptr(), lse.data_ptr()
+            if dh is not None:
+                g.grad_h_acc, g.accumulate_grad_h = dh.data_ptr(), 1 if i > 0 else 0
+            if gW_buf is not None:
+                g.grad_W, g.grad_W_dtype, g.ld_grad_W = gW_buf[v0].data_ptr(), nat.dtype_code(gW_buf.dtype), K8
+            if gE is not None:
+                g.grad_E, g.grad_E_dtype, g.ld_grad_E = gE[v0].data_ptr(), nat.dtype_code(gE.dtype), max(E.shape[1], 1)
+            if gb is not None:
+                g.grad_bias, g.grad_bias_dtype = gb[v0:].data_ptr(), nat.dtype_code(gb.dtype)
+            nbytes = nat.c_size_t(0)
+            nat.check(lib.swvr_bwd_workspace_size(p, g, nat.ctypes.byref(nbytes)), "swvr_bwd_workspace_size")
+            ws = _workspace(nbytes.value, dev)
+            nat.check(lib.swvr_bwd(p, g, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)), "swvr_bwd")
+    if gh is not None:
+        gh.copy_(dh[:, :K])
+    if gW is not None and gW_buf is not gW:
         gW.copy_(gW_buf[:, :K])
     return gh, gW, gE, gb
 

@@ -141,6 +141,26 @@ def test_autocast_with_fp32_params():
         assert rel_err(a, r) < 2e-2
 
 
+def test_autocast_fp32_params_cast_per_chunk():
+    """fp32 parameters under bf16 autocast: W and E are cast to bf16 one vocabulary chunk at a time
+    (the reference's W[v0:v1].to(cdt), chunked.py:90-95), so no whole bf16 copy of W is held."""
+    N, K, V, D, C = 1024, 1024, 131072, 16, 4096
+    h, W, E, b = make_gpu(N, K, V, D, torch.float32)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        O, lse = swvr.softmax_readout(h, W, E, b, chunk_size=C)
+    (O.sum() + lse.sum()).backward()
+    torch.cuda.synchronize()
+    extra = torch.cuda.max_memory_allocated() - base
+    grads = sum(x.numel() * x.element_size() for x in (h, W, E, b))
+    whole_copy = V * K * 2
+    print(f"extra {extra / 2**20:.0f} MiB, grads {grads / 2**20:.0f} MiB, a whole bf16 W {whole_copy / 2**20:.0f} MiB")
+    assert extra < grads + whole_copy // 2
+    assert W.grad.dtype == torch.float32 and torch.isfinite(W.grad).all()
+
+
 def test_bf16_chunk_invariance():
     """test_cuda.py:80-86."""
     inputs = make_gpu(300, 256, 9000, 16, torch.bfloat16)

@@ -18,7 +18,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
     assert set(names) == set(nat._SIGNATURES), "binding table out of sync with the header"
-    assert lib.swvr_abi_version() == 1
+    assert lib.swvr_abi_version() == 2
 
 
 def _problem(N=256, K=64, V=1000, D=16, dt=nat.BF16, ptr=1 << 20, chunk=8192, ld=None):
