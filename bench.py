@@ -372,13 +372,69 @@ def run_reference_arm(args, c, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args, c, rank, world):
+    """--impl reference-gpu: the reference library's own GPU path (its custom ops over cuBLAS and
+    Triton), unmodified, from the offline install in baseline/_ref, on the same inputs and step
+    as ours.  One GPU; rank 0 of a multi-rank launch runs it alone."""
+    if rank != 0:
+        return
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    base = {"metric": metric_name(args, c), "impl": "reference-gpu"}
+    if not os.path.isdir(os.path.join(ref_dir, "swvr")):
+        print(json.dumps({**base, "unavailable": "no offline install of the reference under baseline/_ref"}))
+        return
+    sys.path.insert(0, ref_dir)
+    import swvr as ref
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    h, W, E, b, t, w, _ = make_inputs(c, device, 0, 1)
+    params = [x for x in (h, W, E, b) if x is not None]
+
+    def step():
+        for p in params:
+            p.grad = None
+        loss = ref.softmax_readout_mse(h, W, E, t, b, weight=w, z_loss_weight=c["z"], chunk_size=args.chunk)
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    for p in params:
+        p.grad = None
+    torch.cuda.reset_peak_memory_stats(device)
+    mem0 = torch.cuda.memory_allocated(device)
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        torch.cuda.synchronize(device)
+        clocks.mark_start()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(device)
+        clocks.mark_end()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    print(json.dumps({**base, "value": round(f_algo(c) / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+                      "higher_is_better": True, "dtype": "bf16", "data": "synthetic (same inputs as ours)",
+                      "config": {"workload": f"{args.config}: the reference's softmax_readout_mse fwd+bwd",
+                                 "chunk_size": args.chunk or 8192},
+                      "peak_mem_gib": round((torch.cuda.max_memory_allocated(device) - mem0) / 2 ** 30, 3),
+                      "clocks": clocks.summary(), "reference_version": getattr(ref, "__version__", None)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"],
+                    help="reference: the reference algorithm on the host cores (the reference arm); "
+                         "reference-gpu: the reference library's own GPU path (cuBLAS + Triton) from an "
+                         "offline install under baseline/_ref, as a comparator")
     ap.add_argument("--chunk", type=int, default=None, help="chunk_size (default: the API default, 8192)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -389,6 +445,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, c, rank, world)
+        return
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args, c, rank, world)
         return
     local = int(os.environ.get("LOCAL_RANK", "0"))
     device = torch.device("cuda", local)

@@ -161,6 +161,24 @@ def test_autocast_fp32_params_cast_per_chunk():
     assert W.grad.dtype == torch.float32 and torch.isfinite(W.grad).all()
 
 
+def test_autocast_fp32_params_odd_shapes():
+    """The per-chunk parameter cast with K not a multiple of 8 (zero-padded per chunk), D = 5,
+    fp16 autocast, an fp32 bias and a vocabulary that leaves a ragged last chunk."""
+    N, K, V, D = 300, 100, 5003, 5
+    h, W, E, b = make_gpu(N, K, V, D, torch.float32)
+    g = torch.Generator().manual_seed(9)
+    gO = torch.randn(N, D, generator=g).cuda()
+    glse = (0.1 * torch.randn(N, generator=g)).cuda()
+    with torch.autocast("cuda", dtype=torch.float16):
+        O, lse = swvr.softmax_readout(h, W, E, b, chunk_size=1000, logit_scale=0.7)
+    grads = torch.autograd.grad((O * gO).sum() + (lse * glse).sum(), (h, W, E, b))
+    assert all(x.dtype == torch.float32 for x in grads)
+    Or, lr, gr = oracle_eager(h, W, E, b, 0.7, gO, glse)
+    assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
+    for name, a_, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
+        assert rel_err(a_, r) < 2e-2, (name, rel_err(a_, r))
+
+
 def test_bf16_chunk_invariance():
     """test_cuda.py:80-86."""
     inputs = make_gpu(300, 256, 9000, 16, torch.bfloat16)
