@@ -53,9 +53,6 @@ __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
@@ -100,22 +97,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
-// Error path only (after a bounded wait expired): give in-flight TMA copies and tcgen05
-// MMAs time to land before the CTA releases its TMEM and shared memory.  The MMA thread
-// commits to a spare barrier and waits for it (bounded, ignoring the abort flag); every
-// thread then sleeps briefly so outstanding bulk copies complete.
-__device__ __forceinline__ void drain_after_abort(bool mma_thread, uint64_t* spare) {
-  if (mma_thread) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(spare))
-                 : "memory");
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(spare, 0) && globaltimer() - t0 < 100000000ull) {
-    }
-  }
-  for (int i = 0; i < 20; ++i) __nanosleep(1000000);
-  __syncthreads();
-}
-
 // ------------------------------------------------------------------ fences / named barriers
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -130,13 +111,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled load, no multicast.  x is the innermost (contiguous) coordinate in elements.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
 
 // 2-D tiled store smem -> global (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
@@ -164,18 +138,6 @@ __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// ------------------------------------------------------------------ tcgen05: TMEM
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -214,34 +176,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
          ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// D[tmem] (+)= A[smem] * B[smem]
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// D[tmem] (+)= A[tmem] * B[smem]
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// Arrive (once) on an mbarrier when every tcgen05 op issued so far by this thread is done.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
 
 // ------------------------------------------------------------------ tcgen05: TMEM <-> registers
 // 32 lanes x 32 bit, repeated 32 / 16 times: thread i of the warp gets lane (base + i),
@@ -369,7 +305,10 @@ __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t cta_mask
       : "memory");
 }
 
-// Error path of a 2-SM kernel: like drain_after_abort, with the pair's commit.
+// Error path only (after a bounded wait expired): give in-flight TMA copies and tcgen05
+// MMAs time to land before the pair releases its TMEM and shared memory.  The MMA thread
+// commits to a spare barrier (the pair's commit) and waits for it, bounded and ignoring the
+// abort flag; every thread then sleeps briefly so outstanding bulk copies complete.
 __device__ __forceinline__ void drain_after_abort_pair(bool mma_thread, uint64_t* spare) {
   if (mma_thread) {
     umma2_commit_mc(spare, 1);
@@ -412,11 +351,6 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(r);
-}
-__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return bits_f2(r);
 }
 
