@@ -207,6 +207,16 @@ const char* swvr_last_error(void);
  */
 int swvr_device_error(uint32_t* code);
 
+/*
+ * Self test of the device-side failure path (no counterpart in the reference): launches one
+ * thread that waits, through the same bounded wait as the tensor-core pipelines, on a
+ * barrier that nothing completes, for at most limit_ns (1 ms .. 10 s).  The wait expires, the
+ * kernel records SWVR_SELFTEST_CODE in the device error word and returns; no fault, no
+ * hang.  swvr_device_error() then reports the code and the device stays usable.
+ */
+#define SWVR_SELFTEST_CODE 0x7F01u
+int swvr_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 int swvr_abi_version(void);
 
 #ifdef __cplusplus

@@ -22,6 +22,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, -1, -2, 
 F32, F64, BF16, F16 = 0, 1, 2, 3
 REDUCE_NONE, REDUCE_SUM, REDUCE_MEAN = 0, 1, 2
 MSE_STATS_LEN = 514  # SWVR_MSE_STATS_LEN
+SELFTEST_CODE = 0x7F01  # SWVR_SELFTEST_CODE
 
 DTYPE_CODE = {torch.float32: F32, torch.float64: F64, torch.bfloat16: BF16, torch.float16: F16}
 
@@ -56,6 +57,7 @@ class ProfileRecord(ctypes.Structure):
 
 _SIGNATURES = {
     "swvr_abi_version": (c_int, []),
+    "swvr_selftest_wait_timeout": (c_int, [c_int64, c_void_p]),
     "swvr_last_error": (c_char_p, []),
     "swvr_device_error": (c_int, [POINTER(c_uint32)]),
     "swvr_fwd_workspace_size": (c_int, [POINTER(Problem), POINTER(c_size_t)]),

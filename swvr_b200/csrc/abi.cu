@@ -466,6 +466,14 @@ extern "C" {
 
 int swvr_abi_version(void) { return SWVR_ABI_VERSION; }
 
+int swvr_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  static_assert((kErrSelftest | 1) == SWVR_SELFTEST_CODE, "self-test code");
+  if (limit_ns < 1000000 || limit_ns > 10000000000ll)
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "limit_ns must be within 1 ms .. 10 s");
+  SWVR_CUDA(small::wait_selftest(static_cast<uint64_t>(limit_ns), static_cast<cudaStream_t>(stream)));
+  return SWVR_OK;
+}
+
 const char* swvr_last_error(void) { return t_err.c_str(); }
 
 int swvr_device_error(uint32_t* code) {

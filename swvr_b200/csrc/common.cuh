@@ -21,6 +21,7 @@ enum : uint32_t {
   kErrFwd = 0x100,
   kErrBwdScores = 0x200,
   kErrGemm = 0x300,
+  kErrSelftest = 0x7F00,  // swvr_selftest_wait_timeout
 };
 
 inline size_t dtype_size(int dt) {

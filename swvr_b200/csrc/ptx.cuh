@@ -74,14 +74,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait until the phase with the given parity has completed.  Returns false (after
 // recording `where` in the device error word and setting *abort) on timeout, or at once
 // when another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t where) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t where,
+                                          uint64_t limit_ns = SWVR_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > SWVR_WAIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(&g_device_error, 0u, where);
         *abort = 1;
         return false;

@@ -143,6 +143,27 @@ cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int
                       TS, n_ts, v_begin, rows, tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
 }
 
+// ------------------------------------------------------------------ bounded-wait self test
+// One thread waits on an mbarrier that nothing arrives on, through the same bounded wait the
+// tensor-core pipelines use, so the error path (error word recorded, kernel returns, context
+// usable) can be exercised without a fault or a hang.
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, kErrSelftest | 1, limit_ns);
+}
+
+cudaError_t wait_selftest(uint64_t limit_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ backward prologue
 // delta = rowsum(O * gO) - glse (swvr/chunked.py:112-113) and gO rounded to the compute
 // dtype, zero-padded to DP columns (chunked.py:114).  One warp per row.

@@ -12,6 +12,8 @@ cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, con
 cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int per_t, int NT, int v_begin, int rows,
                          int tile_rows, int64_t D, void* gE, int gE_dt, int64_t ld_gE, void* gb, int gb_dt, bool pdl,
                          cudaStream_t st);
+// Launch a kernel whose bounded wait expires after limit_ns (records kErrSelftest | 1).
+cudaError_t wait_selftest(uint64_t limit_ns, cudaStream_t st);
 cudaError_t prologue(bool bf16, const float* O, const float* gO, const float* glse, int64_t N, int D, int DP,
                      float* delta, void* gOc, cudaStream_t st);
 cudaError_t cast_f32(const float* src, void* dst, int dt, int64_t n, cudaStream_t st);
