@@ -21,6 +21,9 @@
 // 64-byte swizzle; for D <= 128 it is N = 128 with a 128-byte swizzle.
 // dE and db of a unit go to a partial slot; reduce_de_db_kernel (small.cu) sums the token
 // splits of a vocabulary row in a fixed order, so the result is deterministic.
+// From the second chunk on, the launch may overlap the previous chunk's GEMM (programmatic
+// dependent launch): loads and MMAs read inputs only, and the gradient warps wait for the
+// predecessors (pdl_wait) before their first dS or partial-slot store.
 //
 // Replaces the reference's per-chunk recompute GEMM + Triton _bwd_chunk_kernel
 // (swvr/chunked.py:120-131, swvr/triton_kernels.py:76-118).

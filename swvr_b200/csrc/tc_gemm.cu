@@ -14,7 +14,9 @@
 // rows from its TMEM and writes them with TMA: a store for dW (cast to the W dtype) and an
 // element-wise TMA add-reduction into the fp32 dh accumulator.  Both problems share one
 // persistent launch (dW tiles first); chunks run in order, so dh's accumulation order is
-// fixed.
+// fixed.  The launch may overlap the previous kernel's tail (programmatic dependent launch):
+// setup runs at once and the producer waits for the predecessors (pdl_wait) before its
+// first dS load.
 //
 // Replaces the reference's cuBLAS calls gH += mm_acc(gS, W_c) and gW[v0:v1] = mm_acc(gS^T, h)
 // (swvr/chunked.py:146-150).
