@@ -165,8 +165,8 @@ static int validate(const swvr_problem* p) {
       (p->vocab > 0 && p->embed_dim > 0 && !p->E))
     return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL input pointer");
   if (is_tc(p->compute_dtype)) {
-    if (p->embed_dim < 1 || p->embed_dim > 128)
-      return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path supports 1 <= D <= 128, got %lld", (long long)p->embed_dim);
+    if (p->embed_dim < 1 || p->embed_dim > 256)
+      return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path supports 1 <= D <= 256, got %lld", (long long)p->embed_dim);
     if (p->hidden < 8 || (p->hidden % 8) != 0 || (p->ldh % 8) != 0 || (p->ldw % 8) != 0 || (p->lde % 8) != 0)
       return fail(SWVR_ERR_UNSUPPORTED, "tensor-core path needs K and row strides that are multiples of 8 elements");
     if ((reinterpret_cast<uintptr_t>(p->h) | reinterpret_cast<uintptr_t>(p->W) | reinterpret_cast<uintptr_t>(p->E)) & 15u)
@@ -177,7 +177,7 @@ static int validate(const swvr_problem* p) {
 
 // ---------------------------------------------------------------------------- forward plan
 struct FwdPlan {
-  int MT, VT, splits, per, units, pairs;
+  int DP, MT, VT, splits, per, units, pairs;
   size_t off_m2, off_l, off_acc, bytes;
 };
 
@@ -188,7 +188,8 @@ static FwdPlan plan_fwd_units(const swvr_problem& p, int max_splits) {
   FwdPlan f{};
   f.pairs = std::max(1, num_sms() / 2);
   f.MT = static_cast<int>(ceil_div(p.n_tokens, tc::kFwdTokenTile));
-  f.VT = static_cast<int>(ceil_div(p.vocab, tc::kFwdVocabTile));
+  f.DP = p.embed_dim <= 64 ? 64 : (p.embed_dim <= 128 ? 128 : 256);
+  f.VT = static_cast<int>(ceil_div(p.vocab, tc::fwd_vocab_tile(f.DP)));
   int best_s = 1;
   int64_t best_cost = -1;
   const int smax = std::max(1, std::min(std::min(f.VT, 64), max_splits));
@@ -219,8 +220,9 @@ static int tc_fwd_launch(const swvr_problem& p, const FwdPlan& f, char* scratch,
   const bool bf16 = p.compute_dtype == SWVR_BF16;
   tc::FwdMaps maps;
   SWVR_TRY(make_map(&maps.h, p.h, p.compute_dtype, p.hidden, p.n_tokens, p.ldh * 2, 64, 128));
-  SWVR_TRY(make_map(&maps.w, p.W, p.compute_dtype, p.hidden, p.vocab, p.ldw * 2, 64, tc::kFwdVocabTile / 2));
-  SWVR_TRY(make_map(&maps.e, p.E, p.compute_dtype, p.embed_dim, p.vocab, p.lde * 2, 64, tc::kFwdVocabTile));
+  const int BV = tc::fwd_vocab_tile(f.DP);
+  SWVR_TRY(make_map(&maps.w, p.W, p.compute_dtype, p.hidden, p.vocab, p.ldw * 2, 64, BV / 2));
+  SWVR_TRY(make_map(&maps.e, p.E, p.compute_dtype, p.embed_dim, p.vocab, p.lde * 2, 64, BV));
   tc::FwdParams prm{};
   prm.N = static_cast<int>(p.n_tokens);
   prm.K = static_cast<int>(p.hidden);
@@ -239,7 +241,7 @@ static int tc_fwd_launch(const swvr_problem& p, const FwdPlan& f, char* scratch,
   prm.part_acc = reinterpret_cast<float*>(scratch + f.off_acc);
   {
     ProfScope ps(kProfFwd, st);
-    SWVR_CUDA(tc::launch_fwd_kernel(bf16, maps, prm, f.pairs, st));
+    SWVR_CUDA(tc::launch_fwd_kernel(bf16, f.DP, maps, prm, f.pairs, st));
   }
   *out = prm;
   return SWVR_OK;
@@ -286,7 +288,7 @@ struct BwdPlan {
 static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   BwdPlan b{};
   b.sms = num_sms();
-  b.DP = p.embed_dim <= 64 ? 64 : 128;
+  b.DP = p.embed_dim <= 64 ? 64 : (p.embed_dim <= 128 ? 128 : 256);
   b.NT = static_cast<int>(ceil_div(p.n_tokens, 128));
   b.Npad = static_cast<int64_t>(b.NT) * 128;
   // The reference's chunk holds chunk x N fp32 scores; dS here is 16-bit, so the same bytes

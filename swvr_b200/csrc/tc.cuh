@@ -22,16 +22,19 @@ struct FwdParams {
 };
 
 constexpr int kFwdTokenTile = 256;  // tokens per work unit (a CTA pair, 128 per CTA)
-constexpr int kFwdVocabTile = 192;  // vocabulary rows per tile
+
+int fwd_vocab_tile(int DP);  // vocabulary rows per tile: 192 (DP <= 128) or 128 (DP 256)
+int fwd_o_width(int DP);     // the O MMA's N: 128 or 256; each CTA stages half of it
 
 struct FwdMaps {
   CUtensorMap h;  // h, box {64, 128}
-  CUtensorMap w;  // W, box {64, 96} (half a vocabulary tile)
-  CUtensorMap e;  // E, box {64, 192}
+  CUtensorMap w;  // W, box {64, fwd_vocab_tile / 2} (half a vocabulary tile)
+  CUtensorMap e;  // E, box {64, fwd_vocab_tile}
 };
 
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
-cudaError_t launch_fwd_kernel(bool bf16, const FwdMaps& maps, const FwdParams& prm, int max_pairs, cudaStream_t st);
+cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int max_pairs,
+                              cudaStream_t st);
 
 // ------------------------------------------------------------------ backward: scores tile kernel
 struct BwdScoresParams {
@@ -55,10 +58,12 @@ struct BwdScoresMaps {
   CUtensorMap h64;  // h, box {64, 64} (half a token tile)
   CUtensorMap e;    // E, box {64, 128}
   CUtensorMap gok;  // gO in the compute dtype [Npad, DP], box {64, 64}, 128-byte swizzle
-  CUtensorMap gom;  // the same, box {bwd_gom_width(DP), 128}, 64-byte (DP 64) or 128-byte swizzle
+  CUtensorMap gom;  // the same, box {bwd_gom_width(DP), 128}, 64-byte (DP 64) or 128-byte swizzle;
+                    // each CTA stages one box of its half of the columns (two for DP 256)
 };
 
-// Embedding columns of gO each CTA stages as the MN-major dE operand (half the dE MMA N).
+// Embedding columns per box of gO as the MN-major dE operand (each CTA stages half the dE
+// MMA's N: one box, or two for DP 256).
 int bwd_gom_width(int DP);
 
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).

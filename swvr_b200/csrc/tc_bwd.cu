@@ -41,10 +41,16 @@ struct BwdCfg {
   static constexpr int HBOX = 64 * 128;   // 64 rows x 128 bytes
   static constexpr int A_BYTES = KH * BOX;   // this CTA's 128 W rows x 64*KH K
   static constexpr int B_BYTES = KH * HBOX;  // this CTA's 64 h rows x 64*KH K
-  static constexpr int DEN = DP == 64 ? 64 : 128;      // dE MMA N (embedding columns, padded)
+  // D padded to 256: dE needs 256 TMEM columns, so S is single-buffered (the gradient pass
+  // then runs between a tile's S MMAs and the next tile's instead of under them)
+  static constexpr bool kSingleS = DP == 256;
+  static constexpr int DEN = DP == 64 ? 64 : (DP == 128 ? 128 : 256);  // dE MMA N (padded)
   static constexpr int GOM_W = DEN / 2;                // embedding columns of gO this CTA stages for dE
-  static constexpr int GOM_ROW = GOM_W * 2;            // bytes per token row of that copy (64 or 128)
-  static constexpr int GOM_BYTES = 128 * GOM_ROW;      // 128 tokens, MN-major
+  static constexpr int GOM_BW = GOM_W < 64 ? GOM_W : 64;  // columns per box (one swizzle atom)
+  static constexpr int GOM_NB = GOM_W / GOM_BW;        // boxes
+  static constexpr int GOM_ROW = GOM_BW * 2;           // bytes per token row of a box (64 or 128)
+  static constexpr int GOM_BOX = 128 * GOM_ROW;        // 128 tokens, MN-major
+  static constexpr int GOM_BYTES = GOM_NB * GOM_BOX;
   static constexpr int E_BYTES = (DP / 64) * BOX;      // this CTA's 128 E rows x DP
   static constexpr int GOK_BYTES = (DP / 64) * HBOX;   // this CTA's 64 tokens x DP (K-major)
   static constexpr int SMEM_A = 0;
@@ -58,10 +64,10 @@ struct BwdCfg {
   static constexpr int NBAR = 2 * NS + 14;
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
-  static constexpr uint32_t S_COL = 0, DP_COL = 256, DE_COL = 384;
+  static constexpr uint32_t S_COL = 0, DP_COL = kSingleS ? 128 : 256, DE_COL = kSingleS ? 256 : 384;
   static_assert(DE_COL + DEN <= 512, "TMEM budget");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
-  static_assert(DP == 64 || DP == 128, "D padding");
+  static_assert(DP == 64 || DP == 128 || DP == 256, "D padding");
   static_assert(GOM_BYTES % 1024 == 0 && GOK_BYTES % 1024 == 0, "1024-byte alignment");
 };
 
@@ -185,19 +191,31 @@ __global__ void __launch_bounds__(256, 1)
               for (int c = 0; c < DP / 64; ++c)
                 tma_load_2d_pair(smem + Cfg::SMEM_GOK + c * Cfg::HBOX, &tm_gok, gb, c * 64, trow);
             }
-            if (it > it0) {
-              if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+            // MN-major gO: with single-buffered S the tile's dE comes before the next S, so it
+            // is loaded with this tile's K-major copy; otherwise the previous tile's, here
+            const int gom_tile = Cfg::kSingleS ? it : it - 1;
+            if (gom_tile >= it0) {
+              const uint32_t gom_use = Cfg::kSingleS ? g : g - 1u;
+              if (!mbar_wait(gom_empty, (gom_use & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
               if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
-              tma_load_2d_pair(smem + Cfg::SMEM_GOM, &tm_gom, mapa_shared(smem_u32(gom_full), 0),
-                               static_cast<int>(rank) * Cfg::GOM_W, (it - 1) * 128);
+              const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+              for (int c = 0; c < Cfg::GOM_NB; ++c)
+                tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                                 static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, gom_tile * 128);
             }
           }
         }
-        // the unit's last tile: its MN-major gO, once the previous tile's dE has read the buffer
-        if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
-        if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
-        tma_load_2d_pair(smem + Cfg::SMEM_GOM, &tm_gom, mapa_shared(smem_u32(gom_full), 0),
-                         static_cast<int>(rank) * Cfg::GOM_W, (it1 - 1) * 128);
+        if (!Cfg::kSingleS) {
+          // the unit's last tile: its MN-major gO, once the previous tile's dE has read the buffer
+          if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+          if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+          const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+          for (int c = 0; c < Cfg::GOM_NB; ++c)
+            tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                             static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, (it1 - 1) * 128);
+        }
         ++uc;
       }
     }
@@ -220,7 +238,8 @@ __global__ void __launch_bounds__(256, 1)
         if (n <= 0) continue;
         for (int j = 0; j <= n; ++j) {
           if (j < n) {
-            const uint32_t b = g & 1u;
+            // (single-buffered S: the previous tile's dE, issued above, read P before this S)
+            const uint32_t b = Cfg::kSingleS ? 0u : (g & 1u);
             for (int kb = 0; kb < KB; ++kb) {
               if (!mbar_wait(&full[stage], sphase, abort_flag, kErrBwdScores | 5)) goto done;
               const uint64_t sa = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));
@@ -239,7 +258,8 @@ __global__ void __launch_bounds__(256, 1)
             // dP^T = E . dO^T into the single dP buffer: both CTAs' gradient passes of the
             // previous tile must have finished reading it.
             if (j == 0 && !mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 6)) goto done;
-            if (j > 0 && !mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 6))
+            if (!Cfg::kSingleS && j > 0 &&
+                !mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 6))
               goto done;
             if (!mbar_wait(gok_full, g & 1u, abort_flag, kErrBwdScores | 7)) goto done;
             tc_fence_after();
@@ -250,8 +270,25 @@ __global__ void __launch_bounds__(256, 1)
             umma2_commit_mc(gok_empty, 3);
             umma2_commit_mc(dp_full, 3);
             ++g;
+            if (Cfg::kSingleS) {
+              // this tile's gradient pass, then its dE, before the next tile's S overwrites P
+              const uint32_t gg = g - 1u;
+              if (!mbar_wait(&p_ready[0], gg & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+              if (!mbar_wait(gom_full, gg & 1u, abort_flag, kErrBwdScores | 9)) goto done;
+              if (need_de) {
+                const bool first = (j == 0);
+                if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                  umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + ks * 8,
+                           sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BOX, 1024), idDE,
+                           (first && ks == 0) ? 0u : 1u);
+              }
+              umma2_commit_mc(gom_empty, 3);
+            }
           }
-          if (j > 0) {
+          if (!Cfg::kSingleS && j > 0) {
             const uint32_t gg = g - 1u - (j < n ? 1u : 0u);
             if (j == n && !mbar_wait(&p_ready[gg & 1u], (gg >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
             if (!mbar_wait(gom_full, gg & 1u, abort_flag, kErrBwdScores | 9)) goto done;
@@ -262,8 +299,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
               for (int ks = 0; ks < 8; ++ks) {
                 const uint64_t bdesc = Cfg::GOM_ROW == 64
-                                           ? sdesc_sw64(gombase + ks * 16 * 64, Cfg::GOM_BYTES, 512)
-                                           : sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BYTES, 1024);
+                                           ? sdesc_sw64(gombase + ks * 16 * 64, Cfg::GOM_BOX, 512)
+                                           : sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BOX, 1024);
                 umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + (gg & 1u) * 128 + ks * 8, bdesc, idDE,
                          (first && ks == 0) ? 0u : 1u);
               }
@@ -309,8 +346,9 @@ __global__ void __launch_bounds__(256, 1)
           delta_s[r] = t < p.N ? -p.delta[t] : 0.f;
         }
         named_bar_sync(1, 128);
-        const uint32_t b = g & 1u;
-        if (!warp_wait(&s_full[b], (g >> 1) & 1u, abort_flag, kErrBwdScores | 10)) goto done;
+        const uint32_t b = Cfg::kSingleS ? 0u : (g & 1u);
+        const uint32_t s_par = Cfg::kSingleS ? (g & 1u) : ((g >> 1) & 1u);
+        if (!warp_wait(&s_full[b], s_par, abort_flag, kErrBwdScores | 10)) goto done;
         if (!warp_wait(dp_full, g & 1u, abort_flag, kErrBwdScores | 11)) goto done;
         tc_fence_after();
         const uint32_t sbase = trow + Cfg::S_COL + b * 128;
@@ -424,15 +462,18 @@ static cudaError_t launch_bwd(const BwdScoresMaps& m, const BwdScoresParams& prm
   return cudaLaunchKernelEx(&cfg, kern, m.w, m.h64, m.e, m.gok, m.gom, prm);
 }
 
-int bwd_gom_width(int DP) { return DP == 64 ? 32 : 64; }
+int bwd_gom_width(int DP) { return DP == 64 ? 32 : 64; }  // columns per box (DP 256: two boxes per CTA)
 
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
                                      int max_pairs, bool pdl, cudaStream_t st) {
   if (DP == 64)
     return bf16 ? launch_bwd<true, 64, 4, 2>(maps, prm, max_pairs, pdl, st)
                 : launch_bwd<false, 64, 4, 2>(maps, prm, max_pairs, pdl, st);
-  return bf16 ? launch_bwd<true, 128, 3, 2>(maps, prm, max_pairs, pdl, st)
-              : launch_bwd<false, 128, 3, 2>(maps, prm, max_pairs, pdl, st);
+  if (DP == 128)
+    return bf16 ? launch_bwd<true, 128, 3, 2>(maps, prm, max_pairs, pdl, st)
+                : launch_bwd<false, 128, 3, 2>(maps, prm, max_pairs, pdl, st);
+  return bf16 ? launch_bwd<true, 256, 2, 2>(maps, prm, max_pairs, pdl, st)
+              : launch_bwd<false, 256, 2, 2>(maps, prm, max_pairs, pdl, st);
 }
 
 }  // namespace tc

@@ -1,19 +1,20 @@
 // Tensor-core (tcgen05) forward of the softmax readout on sm_100a, 2-SM.
 //
 // A CTA pair (cluster of 2) walks work units (a 256-token tile x a contiguous range of
-// 192-row vocabulary tiles).  Each CTA owns 128 of the tokens (TMEM lanes = token rows).
+// vocabulary tiles of BV rows: 192 for D <= 128, 128 for D <= 256).  Each CTA owns 128 of the tokens (TMEM lanes = token rows).
 // Per vocabulary tile j, with tcgen05.mma.cta_group::2 issued by the even CTA:
-//   S_j  = h_tile . W_j^T            M = 256 tokens, N = 192 rows; each CTA stages its own
-//                                    128 h rows and half (96) of the W rows per K-block
+//   S_j  = h_tile . W_j^T            M = 256 tokens, N = BV rows; each CTA stages its own
+//                                    128 h rows and half of the W rows per K-block
 //   P_j  = 2^(S_j*s*log2e + b*log2e - m_ref), rounded to bf16/fp16 and stored back into
 //          TMEM over S_j (one thread per token row: row max / row sum are thread-local)
-//   O   += P_j . E_j                 A = P from TMEM; B = E_j, N = 128 (each CTA stages 64
-//                                    embedding columns; past D the boxes read zero fill)
+//   O   += P_j . E_j                 A = P from TMEM; B = E_j, N = 128 or 256 (each CTA stages
+//                                    half of the embedding columns; past D the boxes read
+//                                    zero fill)
 // so neither S nor P ever leaves the SM.  A pair moves 28 KB per CTA per 64-wide K-block
 // for 2*256*192*64 FLOP, against 40 KB for a single-CTA 128x192 tile: the L2->SMEM feed,
 // which bounds the single-CTA kernel, drops below the MMA rate.  Warp roles: warp 0 issues
 // TMA loads, warp 1 (one thread, even CTA) issues MMAs, warps 4-7 run the online softmax.
-// S is double-buffered in TMEM (2 x 192 columns, O in the last 128), so the MMAs of tile
+// S is double-buffered in TMEM (2 x BV columns, O in the last 128 or 256), so the MMAs of tile
 // j+1 overlap the softmax of tile j.  The running reference max m_ref is only raised when
 // a chunk's max exceeds it by more than 2^kEmergency (exact either way because l and O
 // share m_ref); then O is rescaled in TMEM.
@@ -30,15 +31,20 @@ namespace swvr {
 namespace tc {
 
 // KH: 64-wide K halves per pipeline stage (8 MMAs per barrier round trip of the MMA thread).
-template <bool kBF16, int NS, int KH>
+// BV: vocabulary rows per tile (the S MMA's N); OW: the O MMA's N (embedding columns padded
+// to 128 or 256; each CTA stages OW / 2 of them as 64-column boxes).  Two S buffers and O
+// share the 512 TMEM columns: (192, 128) for D <= 128, (128, 256) for D <= 256.
+template <bool kBF16, int NS, int KH, int BV_, int OW>
 struct FwdCfg {
-  static constexpr int BV = kFwdVocabTile;   // vocabulary rows per tile (MMA N)
+  static constexpr int BV = BV_;
   static constexpr int HBV = BV / 2;         // W rows staged by each CTA
   static constexpr int BOXA = 128 * 128;     // 128 h rows x 64 K
-  static constexpr int BOXB = HBV * 128;     // 96 W rows x 64 K
+  static constexpr int BOXB = HBV * 128;     // HBV W rows x 64 K
   static constexpr int A_BYTES = KH * BOXA;
   static constexpr int B_BYTES = KH * BOXB;
-  static constexpr int E_BYTES = BV * 128;   // 192 vocabulary rows x this CTA's 64 embedding columns
+  static constexpr int EB = OW / 128;        // 64-column E boxes per CTA
+  static constexpr int E_BOX = BV * 128;     // BV vocabulary rows x 64 embedding columns
+  static constexpr int E_BYTES = EB * E_BOX;
   static constexpr int SMEM_A = 0;
   static constexpr int SMEM_B = SMEM_A + NS * A_BYTES;
   static constexpr int SMEM_E = SMEM_B + NS * B_BYTES;
@@ -48,18 +54,19 @@ struct FwdCfg {
   static constexpr float kEmergency = kBF16 ? 64.f : 8.f;  // max P = 2^kEmergency stays finite in 16 bits
   static constexpr int SMEM_TOTAL = SMEM_BAR + NBAR * 8 + 16;
   static constexpr int SMEM_ALLOC = SMEM_TOTAL + 1024;
-  static constexpr uint32_t O_COL = 2 * BV;  // O: 128 columns (N = 128: 64 embedding columns per CTA)
-  static_assert(O_COL + 128 <= 512, "TMEM budget");
+  static constexpr uint32_t O_COL = 2 * BV;
+  static_assert(O_COL + OW <= 512, "TMEM budget");
+  static_assert(OW == 128 || OW == 256, "O width");
   static_assert(BV % 32 == 0 && HBV % 8 == 0, "vocabulary tile");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
   static_assert(BOXA % 1024 == 0 && BOXB % 1024 == 0 && E_BYTES % 1024 == 0, "1024-byte alignment");
 };
 
-template <bool kBF16, int NS, int KH>
+template <bool kBF16, int NS, int KH, int BV_, int OW>
 __global__ void __launch_bounds__(256, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_w,
                const __grid_constant__ CUtensorMap tm_e, const FwdParams p) {
-  using Cfg = FwdCfg<kBF16, NS, KH>;
+  using Cfg = FwdCfg<kBF16, NS, KH, BV_, OW>;
   constexpr int BV = Cfg::BV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -142,8 +149,11 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t eb = g & 1u, use = g >> 1;
           if (!mbar_wait(&e_empty[eb], (use & 1u) ^ 1u, abort_flag, kErrFwd | 2)) goto done;
           if (leader) mbar_arrive_expect_tx(&e_full[eb], 2 * Cfg::E_BYTES);
-          tma_load_2d_pair(smem + Cfg::SMEM_E + eb * Cfg::E_BYTES, &tm_e, mapa_shared(smem_u32(&e_full[eb]), 0),
-                           static_cast<int>(rank) * 64, vt * BV);
+#pragma unroll
+          for (int c = 0; c < Cfg::EB; ++c)
+            tma_load_2d_pair(smem + Cfg::SMEM_E + eb * Cfg::E_BYTES + c * Cfg::E_BOX, &tm_e,
+                             mapa_shared(smem_u32(&e_full[eb]), 0), static_cast<int>(rank) * (OW / 2) + c * 64,
+                             vt * BV);
         }
       }
     }
@@ -151,7 +161,7 @@ __global__ void __launch_bounds__(256, 1)
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer (leader only)
       const uint32_t idS = idesc_f16(kBF16, 256, BV, false, false);
-      const uint32_t idPE = idesc_f16(kBF16, 256, 128, false, true);
+      const uint32_t idPE = idesc_f16(kBF16, 256, OW, false, true);
       // stage-0 descriptors; a stage / K half / 16-wide K step adds (byte offset >> 4)
       const uint64_t da0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);
       const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
@@ -193,7 +203,7 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t ebase = smem_u32(smem + Cfg::SMEM_E + bb * Cfg::E_BYTES);
 #pragma unroll
             for (int ks = 0; ks < BV / 16; ++ks)
-              umma2_ts(tmem + Cfg::O_COL, tmem + bb * BV + ks * 8, sdesc_sw128(ebase + ks * 2048, Cfg::E_BYTES, 1024),
+              umma2_ts(tmem + Cfg::O_COL, tmem + bb * BV + ks * 8, sdesc_sw128(ebase + ks * 2048, Cfg::E_BOX, 1024),
                        idPE, (first && ks == 0) ? 0u : 1u);
             umma2_commit_mc(pe_done, 3);
             umma2_commit_mc(&e_empty[bb], 3);
@@ -354,10 +364,10 @@ done:
 }
 
 // ------------------------------------------------------------------------------------- host
-template <bool kBF16, int NS, int KH>
+template <bool kBF16, int NS, int KH, int BV, int OW>
 static cudaError_t launch_fwd(const FwdMaps& m, const FwdParams& prm, int max_pairs, cudaStream_t st) {
-  using Cfg = FwdCfg<kBF16, NS, KH>;
-  auto kern = fwd_kernel<kBF16, NS, KH>;
+  using Cfg = FwdCfg<kBF16, NS, KH, BV, OW>;
+  auto kern = fwd_kernel<kBF16, NS, KH, BV, OW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -381,8 +391,16 @@ static cudaError_t launch_fwd(const FwdMaps& m, const FwdParams& prm, int max_pa
   return cudaLaunchKernelEx(&cfg, kern, m.h, m.w, m.e, prm);
 }
 
-cudaError_t launch_fwd_kernel(bool bf16, const FwdMaps& maps, const FwdParams& prm, int max_pairs, cudaStream_t st) {
-  return bf16 ? launch_fwd<true, 3, 2>(maps, prm, max_pairs, st) : launch_fwd<false, 3, 2>(maps, prm, max_pairs, st);
+int fwd_vocab_tile(int DP) { return DP <= 128 ? 192 : 128; }
+int fwd_o_width(int DP) { return DP <= 128 ? 128 : 256; }
+
+cudaError_t launch_fwd_kernel(bool bf16, int DP, const FwdMaps& maps, const FwdParams& prm, int max_pairs,
+                              cudaStream_t st) {
+  if (DP <= 128)
+    return bf16 ? launch_fwd<true, 3, 2, 192, 128>(maps, prm, max_pairs, st)
+                : launch_fwd<false, 3, 2, 192, 128>(maps, prm, max_pairs, st);
+  return bf16 ? launch_fwd<true, 3, 2, 128, 256>(maps, prm, max_pairs, st)
+              : launch_fwd<false, 3, 2, 128, 256>(maps, prm, max_pairs, st);
 }
 
 }  // namespace tc

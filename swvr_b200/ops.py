@@ -38,13 +38,14 @@ def _tensor_core(cdt: torch.dtype) -> bool:
     return cdt in (torch.bfloat16, torch.float16)
 
 
-TC_MAX_D = 128  # widest embedding of the tensor-core kernels (O / dE accumulators in TMEM)
+TC_MAX_D = 256  # widest embedding of the tensor-core kernels (O / dE accumulators in TMEM)
 
 
 def _engine_dtype(cdt: torch.dtype, D: int) -> torch.dtype:
     """The dtype the library computes in.  bf16 / fp16 run the tensor-core kernels up to
-    D = 128; wider embeddings (the reference accepts any D) run the exact fp32 SIMT kernels on
-    fp32 copies of the operands, which is at least as accurate as the 16-bit contract."""
+    D = 256 (the reference's Triton path covers the same range); wider embeddings (the
+    reference accepts any D) run the exact fp32 SIMT kernels on fp32 copies of the operands,
+    which is at least as accurate as the 16-bit contract."""
     return torch.float32 if _tensor_core(cdt) and D > TC_MAX_D else cdt
 
 

@@ -92,10 +92,10 @@ def test_golden_bf16(name):
 # ------------------------------------------------------------------------------ test_cuda.py contracts
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("chunk", [1024, 3000])
-@pytest.mark.parametrize("D", [5, 16, 128, 200])
+@pytest.mark.parametrize("D", [5, 16, 128, 200, 256])
 def test_low_precision_matches_fp64(dtype, chunk, D):
-    """test_cuda.py:37-54 with the fp64 numpy oracle as the checker (D = 200 runs the fp32 SIMT
-    kernels: the tensor-core kernels stop at D = 128)."""
+    """test_cuda.py:37-54 with the fp64 numpy oracle as the checker (D = 200 and 256 run the
+    tensor-core variant for D <= 256: single-buffered scores in the backward)."""
     N, K, V = 517, 512, 10007
     inputs = make_gpu(N, K, V, D, dtype)
     g = torch.Generator().manual_seed(3)
@@ -177,6 +177,23 @@ def test_autocast_fp32_params_odd_shapes():
     assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
     for name, a_, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
         assert rel_err(a_, r) < 2e-2, (name, rel_err(a_, r))
+
+
+def test_wide_embedding_runs_simt():
+    """D > 256 in bf16: the tensor-core kernels stop at 256, so the exact fp32 SIMT kernels run on
+    fp32 copies of the operands; results still match the oracle within the 16-bit tolerance."""
+    N, K, V, D = 200, 128, 2000, 300
+    inputs = make_gpu(N, K, V, D, torch.bfloat16)
+    g = torch.Generator().manual_seed(4)
+    gO = torch.randn(N, D, generator=g).cuda()
+    glse = (0.1 * torch.randn(N, generator=g)).cuda()
+    O, lse = swvr.softmax_readout(*inputs, chunk_size=700)
+    grads = torch.autograd.grad((O * gO).sum() + (lse * glse).sum(), inputs)
+    Or, lr, gr = oracle_eager(*inputs, 1.0, gO, glse)
+    assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
+    for name, a_, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
+        assert rel_err(a_, r) < 2e-2, (name, rel_err(a_, r))
+    assert all(x.dtype == torch.bfloat16 for x in grads)
 
 
 def test_bf16_chunk_invariance():

@@ -49,7 +49,7 @@ def test_workspace_planning_without_a_gpu():
     (dict(N=-1), nat.ERR_INVALID_ARGUMENT),
     (dict(chunk=0), nat.ERR_INVALID_ARGUMENT),
     (dict(dt=7), nat.ERR_INVALID_ARGUMENT),
-    (dict(D=200), nat.ERR_UNSUPPORTED),          # tensor-core path: D <= 128
+    (dict(D=300), nat.ERR_UNSUPPORTED),          # tensor-core path: D <= 256
     (dict(K=12), nat.ERR_UNSUPPORTED),           # tensor-core path: K multiple of 8
     (dict(ptr=(1 << 20) + 2), nat.ERR_UNSUPPORTED),  # 16-byte alignment
     (dict(ld=32), nat.ERR_INVALID_ARGUMENT),     # row stride shorter than the row
