@@ -39,6 +39,8 @@ CONFIGS = {
     "c1": dict(N=16384, K=1024, V=152064, D=16, bias=False, weight=None, z=0.0),
     "c2": dict(N=16384, K=2560, V=152064, D=64, bias=True, weight=0.9, z=1e-4),
     "c3": dict(N=8192, K=4096, V=128256, D=128, bias=False, weight=None, z=0.0),
+    # the headline shape with the widest embedding the tensor-core kernels take
+    "d256": dict(N=16384, K=2560, V=152064, D=256, bias=True, weight=0.9, z=1e-4),
     # large batch under activation checkpointing (the readout's forward re-runs in the backward),
     # meant for 2/4/8 GPUs; F_exec counts the re-run, F_algo does not
     "c4": dict(N=131072, K=4096, V=152064, D=64, bias=True, weight=None, z=0.0, checkpoint=True),
