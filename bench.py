@@ -473,6 +473,9 @@ def main():
                 v[1] for v in r["prof"].values())), 4)}
             if fl:
                 kernels[name]["algo_tflops"] = round(fl / (avg * 1e-3) / 1e12, 1)
+            if name == "bwd_scores_kernel":  # with the S recompute, which F_algo leaves out
+                ex = 2.0 * c["N"] * r["Vr"] * c["K"] / per_step[name] + (fl or 0.0)
+                kernels[name]["exec_tflops"] = round(ex / (avg * 1e-3) / 1e12, 1)
         dom = max(r["prof"].items(), key=lambda kv: kv[1][1])[0]
         dom_fl = kernel_flops(dom, c, r["Vr"], per_step[dom], args.chunk)
         dom_avg = r["prof"][dom][1] / r["prof"][dom][0]
