@@ -27,7 +27,7 @@ def _problem(N=256, K=64, V=1000, D=16, dt=nat.BF16, ptr=1 << 20, chunk=8192, ld
     p.compute_dtype, p.bias_dtype = dt, nat.F32
     p.h = p.W = p.E = ptr
     p.ldh = p.ldw = ld or K
-    p.lde = max(D, 8) if dt in (nat.BF16, nat.F16) else D
+    p.lde = (max(D, 8) + 7) // 8 * 8 if dt in (nat.BF16, nat.F16) else D  # pitch as ops._operand pads it
     p.logit_scale, p.chunk = 1.0, chunk
     return p
 
@@ -126,3 +126,27 @@ def test_module_holds_references():
     assert swvr.__version__ == "0.1.0"
     assert set(swvr.__all__) == {"softmax_readout", "softmax_readout_mse", "SoftmaxReadoutMSE",
                                  "softmax_readout_reference"}
+
+
+def test_wide_embedding_and_chunk_planning():
+    """D up to 256 plans on the tensor-core path (257 is rejected); backward chunks are balanced:
+    19008 rows (one shard of c2 on 8 GPUs) at chunk_size 8192 are two chunks of 9728, not
+    16384 + 2624, so the dS buffer is sized for 9728 rows."""
+    lib = nat.lib()
+    nbytes = ctypes.c_size_t(0)
+    for D in (129, 200, 256):
+        assert lib.swvr_fwd_workspace_size(_problem(N=1000, K=512, V=5000, D=D), ctypes.byref(nbytes)) == nat.OK
+    assert lib.swvr_fwd_workspace_size(_problem(D=257), ctypes.byref(nbytes)) == nat.ERR_UNSUPPORTED
+    g = nat.Grads()
+    g.grad_h, g.grad_W, g.grad_E = 1 << 20, 1 << 20, 1 << 20
+    N = 16384
+    assert lib.swvr_bwd_workspace_size(_problem(N=N, K=2560, V=19008, D=64), g, ctypes.byref(nbytes)) == nat.OK
+    dS_balanced = 9728 * N * 2
+    assert dS_balanced < nbytes.value < 16384 * N * 2
+
+
+def test_selftest_limits_are_checked_on_the_host():
+    lib = nat.lib()
+    assert lib.swvr_selftest_wait_timeout(10, None) == nat.ERR_INVALID_ARGUMENT
+    assert lib.swvr_selftest_wait_timeout(20_000_000_000, None) == nat.ERR_INVALID_ARGUMENT
+    assert "limit_ns" in nat.last_error()
