@@ -141,8 +141,8 @@ def test_wide_embedding_and_chunk_planning():
     g.grad_h, g.grad_W, g.grad_E = 1 << 20, 1 << 20, 1 << 20
     N = 16384
     assert lib.swvr_bwd_workspace_size(_problem(N=N, K=2560, V=19008, D=64), g, ctypes.byref(nbytes)) == nat.OK
-    dS_balanced = 9728 * N * 2
-    assert dS_balanced < nbytes.value < 16384 * N * 2
+    dh = N * 2560 * 4                       # the fp32 dh accumulator shares the workspace
+    assert 9728 * N * 2 + dh < nbytes.value < 16384 * N * 2 + dh
 
 
 def test_selftest_limits_are_checked_on_the_host():
