@@ -10,55 +10,92 @@
 namespace swvr {
 namespace simt {
 
-constexpr int TM = 64, TN = 64, TK = 16;
+// C[m, n] = alpha * sum_k A[m, k] B[k, n] + beta * C[m, n] with arbitrary strides (the callers
+// pass transposes as strides) and C of any dtype.  128 x 128 block tiles, 8-deep K steps,
+// 8 x 8 outputs per thread; the next K step's tiles are fetched into registers while the
+// current one is multiplied.  Global loads run along whichever dimension of A / B has unit
+// stride, so they coalesce for row- and column-major operands alike.
+constexpr int BM = 128, BN = 128, BK = 8, PAD = 4;
 
-// C[m, n] = alpha * sum_k A[m, k] B[k, n] + beta * C[m, n]; arbitrary strides, C of any dtype.
+template <typename T>
+struct GemmTileLoader {
+  // one thread's 4 elements of the BM x BK tile of A and of the BK x BN tile of B
+  T a[4], b[4];
+  __device__ __forceinline__ void load(const T* __restrict__ A, int64_t sam, int64_t sak, const T* __restrict__ B,
+                                       int64_t sbk, int64_t sbn, int64_t M, int64_t N, int64_t K, int64_t m0,
+                                       int64_t n0, int64_t k0, int t) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int64_t m, k;
+      if (sak == 1) { m = m0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous in A
+      else          { m = m0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // M contiguous (or general)
+      a[e] = (m < M && k < K) ? A[m * sam + k * sak] : T(0);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int64_t n, k;
+      if (sbn == 1) { n = n0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // N contiguous in B
+      else          { n = n0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous (or general)
+      b[e] = (n < N && k < K) ? B[k * sbk + n * sbn] : T(0);
+    }
+  }
+  __device__ __forceinline__ void store(T (*As)[BM + PAD], T (*Bs)[BN + PAD], bool a_kcontig, bool b_ncontig,
+                                        int t) const {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (a_kcontig) As[(t % 2) * 4 + e][t / 2] = a[e];
+      else As[t / 32][(t % 32) * 4 + e] = a[e];
+      if (b_ncontig) Bs[t / 32][(t % 32) * 4 + e] = b[e];
+      else Bs[(t % 2) * 4 + e][t / 2] = b[e];
+    }
+  }
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_kernel(int64_t M, int64_t N, int64_t K, T alpha, const T* __restrict__ A,
                                                    int64_t sam, int64_t sak, const T* __restrict__ B, int64_t sbk,
                                                    int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn) {
-  __shared__ T As[TK][TM + 1];
-  __shared__ T Bs[TK][TN + 1];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * TM, n0 = static_cast<int64_t>(blockIdx.x) * TN;
-  T acc[4][4];
+  __shared__ __align__(16) T As[BK][BM + PAD];
+  __shared__ __align__(16) T Bs[BK][BN + PAD];
+  const int t = threadIdx.x, tx = t % 16, ty = t / 16;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM, n0 = static_cast<int64_t>(blockIdx.x) * BN;
+  const bool a_kcontig = sak == 1, b_ncontig = sbn == 1;
+  T acc[8][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = T(0);
-  for (int64_t k0 = 0; k0 < K; k0 += TK) {
-    for (int idx = threadIdx.x; idx < TK * TM; idx += 256) {
-      const int kk = idx / TM, mm = idx % TM;
-      const int64_t gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < M && gk < K) ? A[gm * sam + gk * sak] : T(0);
-    }
-    for (int idx = threadIdx.x; idx < TK * TN; idx += 256) {
-      const int kk = idx / TN, nn = idx % TN;
-      const int64_t gn = n0 + nn, gk = k0 + kk;
-      Bs[kk][nn] = (gn < N && gk < K) ? B[gk * sbk + gn * sbn] : T(0);
-    }
+    for (int j = 0; j < 8; ++j) acc[i][j] = T(0);
+  GemmTileLoader<T> ld;
+  ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, 0, t);
+  for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    __syncthreads();  // the previous step's reads of As / Bs are done
+    ld.store(As, Bs, a_kcontig, b_ncontig, t);
     __syncthreads();
+    if (k0 + BK < K) ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, k0 + BK, t);
 #pragma unroll
-    for (int kk = 0; kk < TK; ++kk) {
-      T a[4], b[4];
+    for (int kk = 0; kk < BK; ++kk) {
+      // rows ty*4 + {0..3} and 64 + ty*4 + {0..3}; columns tx*4 + {0..3} and 64 + tx*4 + {0..3}
+      T a[8], b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[kk][ty * 4 + i];
+        a[4 + i] = As[kk][64 + ty * 4 + i];
+        b[i] = Bs[kk][tx * 4 + i];
+        b[4 + i] = Bs[kk][64 + tx * 4 + i];
+      }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+        for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
     }
-    __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t gm = m0 + ty + 16 * i;
+  for (int i = 0; i < 8; ++i) {
+    const int64_t gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
     if (gm >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t gn = n0 + tx + 16 * j;
+    for (int j = 0; j < 8; ++j) {
+      const int64_t gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
       if (gn >= N) continue;
       const int64_t off = gm * scm + gn * scn;
       T v = alpha * acc[i][j];
@@ -72,7 +109,7 @@ template <typename T>
 cudaError_t gemm(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, const T* A, int64_t sam, int64_t sak,
                  const T* B, int64_t sbk, int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn) {
   if (M == 0 || N == 0) return cudaSuccess;
-  dim3 grid(static_cast<unsigned>(ceil_div(N, TN)), static_cast<unsigned>(ceil_div(M, TM)));
+  dim3 grid(static_cast<unsigned>(ceil_div(N, BN)), static_cast<unsigned>(ceil_div(M, BM)));
   gemm_kernel<T><<<grid, 256, 0, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn);
   return cudaGetLastError();
 }
