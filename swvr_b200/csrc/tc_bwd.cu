@@ -11,14 +11,17 @@
 // All three products are tcgen05.mma.cta_group::2 issued by the even CTA: each CTA stages
 // its own 128 W rows and half of the h tile (64 tokens), so a pair moves 24 KB per CTA per
 // 64-wide K-block for 2*256*128*64 FLOP.  The W / h ring has 4 stages of 128-wide K-blocks
-// for D <= 64 (3 for D <= 128): the MMAs of a stage take ~512 cycles and the L2 latency of
-// the TMA loads under load is about three stages of that.
+// for D <= 64 (3 for D <= 128, 2 for D <= 256): the MMAs of a stage take ~512 cycles and the
+// L2 latency of the TMA loads under load is about three stages of that.
 // gO is staged twice per token tile, each copy single-buffered with its own barriers: the
 // CTA's 64-token half, K-major, as the B operand of dP^T (loaded early in the tile's S
 // K-loop, after the previous dP has completed), and the CTA's half of the embedding
 // columns of all 128 tokens, MN-major, as the B operand of dE (loaded one tile later, after
 // the previous dE).  For D <= 64 dE is N = 64 and the MN-major copy is 32 columns wide with a
-// 64-byte swizzle; for D <= 128 it is N = 128 with a 128-byte swizzle.
+// 64-byte swizzle; for D <= 128 it is N = 128 with a 128-byte swizzle.  For D <= 256 dE is
+// N = 256 (two 64-column boxes per CTA) and takes 256 TMEM columns, so S is single-buffered:
+// a tile's gradient pass and its dE run before the next tile's S MMAs, and the MN-major gO
+// is loaded with the tile's own K-major copy.
 // dE and db of a unit go to a partial slot; reduce_de_db_kernel (small.cu) sums the token
 // splits of a vocabulary row in a fixed order, so the result is deterministic.
 // From the second chunk on, the launch may overlap the previous chunk's GEMM (programmatic

@@ -1,7 +1,8 @@
 // Tensor-core (tcgen05) forward of the softmax readout on sm_100a, 2-SM.
 //
 // A CTA pair (cluster of 2) walks work units (a 256-token tile x a contiguous range of
-// vocabulary tiles of BV rows: 192 for D <= 128, 128 for D <= 256).  Each CTA owns 128 of the tokens (TMEM lanes = token rows).
+// vocabulary tiles of BV rows: 192 for D <= 128, 128 for D <= 256).  Each CTA owns 128 of the
+// tokens (TMEM lanes = token rows).
 // Per vocabulary tile j, with tcgen05.mma.cta_group::2 issued by the even CTA:
 //   S_j  = h_tile . W_j^T            M = 256 tokens, N = BV rows; each CTA stages its own
 //                                    128 h rows and half of the W rows per K-block
