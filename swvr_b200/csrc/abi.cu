@@ -278,7 +278,7 @@ static void choose_ts(int VTc, int NT, int sms, int* TS, int* per_t) {
 }
 
 struct BwdPlan {
-  int DP, NT, C, sms;
+  int DP, BN, NT, C, sms;
   int64_t Npad;
   bool need_h, need_W, need_E, need_b, need_ds;
   size_t off_delta, off_goc, off_ds, off_dh, off_de, off_db, bytes;
@@ -289,8 +289,9 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   BwdPlan b{};
   b.sms = num_sms();
   b.DP = p.embed_dim <= 64 ? 64 : (p.embed_dim <= 128 ? 128 : 256);
-  b.NT = static_cast<int>(ceil_div(p.n_tokens, 128));
-  b.Npad = static_cast<int64_t>(b.NT) * 128;
+  b.BN = tc::bwd_token_tile(b.DP, p.hidden);
+  b.NT = static_cast<int>(ceil_div(p.n_tokens, b.BN));
+  b.Npad = static_cast<int64_t>(b.NT) * b.BN;  // a multiple of 64 (the GEMMs' token K-blocks)
   // The reference's chunk holds chunk x N fp32 scores; dS here is 16-bit, so the same bytes
   // hold 2 * chunk rows.  A multiple of 256 so that only the last chunk has a partial
   // 256-row pair tile.
@@ -367,11 +368,11 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
 
   tc::BwdScoresMaps sm;
   SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));
-  SWVR_TRY(make_map(&sm.h64, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
+  SWVR_TRY(make_map(&sm.h, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, b.BN / 2));
   SWVR_TRY(make_map(&sm.e, p.E, p.compute_dtype, D, V, p.lde * 2, 64, 128));
-  SWVR_TRY(make_map(&sm.gok, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, 64));
+  SWVR_TRY(make_map(&sm.gok, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, tc::bwd_dp_chunk(b.BN) / 2));
   const int gomw = tc::bwd_gom_width(b.DP);
-  SWVR_TRY(make_map(&sm.gom, goc, p.compute_dtype, b.DP, N, b.DP * 2, gomw, 128, gomw * 2));
+  SWVR_TRY(make_map(&sm.gom, goc, p.compute_dtype, b.DP, N, b.DP * 2, gomw, b.BN, gomw * 2));
   tc::GemmMaps gm;
   if (b.need_ds) {
     SWVR_TRY(make_map(&gm.h_mn, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
@@ -424,7 +425,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     {
       ProfScope ps(kProfBwdScores, st);
       // after the first chunk the previous kernel in the stream is this loop's own
-      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
+      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, b.BN, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
     }
     if (part_de || part_db) {
       void* gE = g.grad_E;

@@ -45,9 +45,9 @@ struct BwdScoresParams {
   int bias_dt;
   const float* lse;    // [N]
   const float* delta;  // [N]
-  int NT, VT;          // 128-token tiles, 256-row vocabulary pair tiles of the chunk
+  int NT, VT;          // BN-token tiles, 256-row vocabulary pair tiles of the chunk
   int TS, per_t, units;  // token splits, token tiles per split, VT * TS
-  void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null (ld_ds >= NT*128)
+  void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null (ld_ds >= NT*BN)
   int64_t ld_ds;
   float* part_de;      // [units * 256 * D] or null
   float* part_db;      // [units * 256] or null
@@ -55,12 +55,20 @@ struct BwdScoresParams {
 
 struct BwdScoresMaps {
   CUtensorMap w;    // W, box {64, 128}
-  CUtensorMap h64;  // h, box {64, 64} (half a token tile)
+  CUtensorMap h;    // h, box {64, BN / 2} (half a token tile)
   CUtensorMap e;    // E, box {64, 128}
-  CUtensorMap gok;  // gO in the compute dtype [Npad, DP], box {64, 64}, 128-byte swizzle
-  CUtensorMap gom;  // the same, box {bwd_gom_width(DP), 128}, 64-byte (DP 64) or 128-byte swizzle;
+  CUtensorMap gok;  // gO in the compute dtype [Npad, DP], box {64, bwd_dp_chunk(BN) / 2}, 128-byte swizzle
+  CUtensorMap gom;  // the same, box {bwd_gom_width(DP), BN}, 64-byte (DP 64) or 128-byte swizzle;
                     // each CTA stages one box of its half of the columns (two for DP 256)
 };
+
+// Tokens per score tile (BN): 192 for DP 64 with K >= 1024, else 128 (the environment
+// variable SWVR_BWD_TOKEN_TILE = 128 or 192 overrides it where that tile exists).
+int bwd_token_tile(int DP, int64_t K);
+
+// Tokens per dP^T chunk: 64 for 192-token tiles (the TMEM left beside two S buffers and
+// dE), else the whole tile.
+__host__ __device__ constexpr int bwd_dp_chunk(int BN) { return BN == 192 ? 64 : BN; }
 
 // Embedding columns per box of gO as the MN-major dE operand (each CTA stages half the dE
 // MMA's N: one box, or two for DP 256).
@@ -69,8 +77,8 @@ int bwd_gom_width(int DP);
 // Launches clusters of 2 CTAs (at most max_pairs pairs, and no more than can be co-resident).
 // pdl: launch with programmatic stream serialization (the previous kernel in the stream is
 // one of ours whose reads of dS / the partial slots this kernel's stores wait for).
-cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                     int max_pairs, bool pdl, cudaStream_t st);
+cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, int BN, const BwdScoresMaps& maps,
+                                     const BwdScoresParams& prm, int max_pairs, bool pdl, cudaStream_t st);
 
 // ------------------------------------------------------------------ backward: dW / dh GEMMs
 struct GemmParams {

@@ -493,3 +493,43 @@ def test_tensor_core_tails(N, K, V, D, dtype):
     assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
     for n, a, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
         assert rel_err(a, r) < 2e-2, (n, rel_err(a, r))
+
+
+# ------------------------------------------------------------------------------ backward score tiles
+@pytest.mark.parametrize("N,K,V,D", [(1, 64, 300, 64), (191, 136, 385, 16), (193, 256, 1000, 64),
+                                     (1000, 1024, 5003, 40)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_backward_192_token_tiles(monkeypatch, N, K, V, D, dtype):
+    """192-token score tiles (dP^T in three 64-token chunks), forced on small shapes: a single
+    token, ragged last token tiles, vocabulary tails, D below 64."""
+    monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", "192")
+    inputs = make_gpu(N, K, V, D, dtype)
+    g = torch.Generator().manual_seed(12)
+    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
+    O, lse = swvr.softmax_readout(*inputs, chunk_size=512, logit_scale=0.7)
+    grads = torch.autograd.grad((O * gO).sum() + (lse * glse).sum(), inputs)
+    Or, lr, gr = oracle_eager(*inputs, 0.7, gO, glse)
+    assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
+    for n, a, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
+        assert rel_err(a, r) < 2e-2, (n, rel_err(a, r))
+
+
+@pytest.mark.parametrize("N,K,V,D,chunk", [(8192, 1024, 8192, 64, 4096), (3000, 2048, 3001, 40, 8192)])
+def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
+    """128- and 192-token score tiles on units of many token tiles (a tile's later dP^T chunks
+    are issued during the next tile's S K-loop).  Both compute the same S, P and dS, and the
+    GEMMs only add zero token blocks, so dh and dW agree bit for bit; dE and db sum the same
+    terms grouped by different token tiles."""
+    inputs = make_gpu(N, K, V, D, torch.bfloat16)
+    g = torch.Generator().manual_seed(13)
+    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
+    res = {}
+    for tile in ("128", "192"):
+        monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", tile)
+        xs = [x.detach().clone().requires_grad_(True) for x in inputs]
+        O, lse = swvr.softmax_readout(*xs, chunk_size=chunk)
+        torch.autograd.backward([O, lse], [gO, glse])
+        res[tile] = [x.grad for x in xs]
+    a, b = res["128"], res["192"]
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    assert rel_err(b[2], a[2]) < 1e-3 and rel_err(b[3], a[3]) < 1e-3
