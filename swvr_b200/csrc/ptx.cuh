@@ -265,6 +265,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// The same without release semantics, for signals that tensor-memory reads or writes have
+// completed (after tcgen05.wait::ld / ::st and tcgen05.fence::before_thread_sync): the
+// waiter only reuses tensor memory, and a cluster-scope release would make the arriving
+// thread wait until every earlier global store of the CTA's threads has reached L2.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // 2-D tiled load into this CTA's shared memory whose completion is counted on an mbarrier
 // of either CTA of the pair (cluster address); no multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
@@ -334,6 +342,22 @@ __device__ __forceinline__ void drain_after_abort_pair(bool mma_thread, uint64_t
 }
 
 // ------------------------------------------------------------------ math helpers
+// Columns [c0, c0 + 32) of a row of D floats (a thread's partial-state row): 16-byte
+// stores when the block is whole and D keeps rows 16-byte aligned, else one float at a time.
+__device__ __forceinline__ void store_row32(float* row, int c0, int D, const uint32_t (&v)[32]) {
+  if ((D & 3) == 0 && c0 + 32 <= D) {
+    float4* d4 = reinterpret_cast<float4*>(row + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]), __uint_as_float(v[4 * i + 2]),
+                          __uint_as_float(v[4 * i + 3]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (c0 + i < D) row[c0 + i] = __uint_as_float(v[i]);
+  }
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

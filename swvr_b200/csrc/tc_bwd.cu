@@ -457,8 +457,8 @@ __global__ void __launch_bounds__(256, 1)
           tc_fence_before();
           named_bar_sync(1, 128);
           if (r == 0) {
-            mbar_arrive_cluster(dp_free_leader);
-            if (last) mbar_arrive_cluster(p_ready_leader + b * 8);
+            mbar_arrive_cluster_relaxed(dp_free_leader);
+            if (last) mbar_arrive_cluster_relaxed(p_ready_leader + b * 8);
           }
         }
       }
@@ -471,17 +471,11 @@ __global__ void __launch_bounds__(256, 1)
           uint32_t o[32];
           tmem_ld32(trow + Cfg::DE_COL + c * 32, o);
           tmem_wait_ld();
-          if (vvalid) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int d = c * 32 + i;
-              if (d < p.D) p.part_de[slot * p.D + d] = __uint_as_float(o[i]);
-            }
-          }
+          if (vvalid) store_row32(p.part_de + slot * p.D, c * 32, p.D, o);
         }
         tc_fence_before();
         named_bar_sync(1, 128);
-        if (r == 0) mbar_arrive_cluster(de_free_leader);
+        if (r == 0) mbar_arrive_cluster_relaxed(de_free_leader);
       }
       if (need_db && vvalid) p.part_db[slot] = db.x + db.y;
       ++uc;

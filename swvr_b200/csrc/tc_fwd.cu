@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(256, 1)
         tmem_wait_st();
         tc_fence_before();
         named_bar_sync(1, 128);
-        if (r == 0) mbar_arrive_cluster(p_ready_leader + b * 8);
+        if (r == 0) mbar_arrive_cluster_relaxed(p_ready_leader + b * 8);
       }
       // unit end: wait for the last P.E, then write this unit's partial state
       if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 9)) goto done;
@@ -335,17 +335,11 @@ __global__ void __launch_bounds__(256, 1)
           uint32_t o[32];
           tmem_ld32(trow + Cfg::O_COL + c, o);
           tmem_wait_ld();
-          if (n < p.N) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int d = c + i;
-              if (d < p.D) p.part_acc[slot * p.D + d] = __uint_as_float(o[i]);
-            }
-          }
+          if (n < p.N) store_row32(p.part_acc + slot * p.D, c, p.D, o);
         }
         tc_fence_before();
         named_bar_sync(1, 128);
-        if (r == 0) mbar_arrive_cluster(o_free_leader);
+        if (r == 0) mbar_arrive_cluster_relaxed(o_free_leader);
         if (n < p.N) {
           p.part_m2[slot] = ref;
           p.part_l[slot] = l;
