@@ -25,6 +25,11 @@
 //    both CTAs' gradient passes have read the previous chunk (a non-blocking barrier test
 //    between K stages).  The K-major gO copy is double-buffered, because the last chunk of a
 //    tile is issued during the next tile's loads.  3 stages.
+// With two S buffers the pair's tiles form one sequence across its units: tile g's S loop
+// runs while the gradient warps process tile g-1, also when g-1 closes the previous unit
+// (its remaining dP chunks are issued during g's S loop and its dE after it), so no unit
+// boundary drains the pipeline.  E is single-buffered: a unit's E is loaded at the last
+// stage of its first tile, after the previous unit's last dP chunk has completed.
 // gO is staged twice per token tile: the CTA's half of each dP chunk's tokens, K-major, as
 // the B operand of dP^T (loaded during the tile's S K-loop), and the CTA's half of the
 // embedding columns of all BN tokens, MN-major, as the B operand of dE (single-buffered,
@@ -167,15 +172,16 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tmem = *tmem_holder;
   if (threadIdx.x == 0) pdl_trigger();
   const int KB = (p.K + 64 * KH - 1) / (64 * KH);  // pipeline stages per S tile
-  const int kx = min(NS, KB - 1);                  // stage after which a tile's E / gO loads are issued
+  const int kx = min(NS, KB - 1);                  // stage after which a tile's gO loads are issued
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer (both CTAs)
-      // E, gO (K-major) of tile i and gO (MN-major) of tile i-1 are loaded after stage kx of
-      // tile i's W / h loads: by then the MMAs that last read those buffers have completed
-      // (in-order MMA execution), so the waits below do not stall the W / h stream.
+      // gO (K-major) of tile i and gO (MN-major) of the tile before it are loaded after stage
+      // kx of tile i's W / h loads: by then the MMAs that last read those buffers have
+      // completed (in-order MMA execution), so the waits below do not stall the W / h stream.
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
+      int prev_it = 0;  // token tile of the previous tile of this pair (double-buffered S)
       for (int u = pair; u < p.units; u += npairs) {
         const int vt = u / p.TS, ts = u % p.TS;
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
@@ -197,8 +203,41 @@ __global__ void __launch_bounds__(256, 1)
               stage = 0;
               sphase ^= 1u;
             }
-            if (kb != kx) continue;
-            if (it == it0) {
+            if (kb == kx) {
+              {
+                // gO, K-major: this CTA's DPC/2 tokens of each dP chunk
+                const uint32_t kbuf = g % Cfg::GOK_NB;
+                if (!mbar_wait(&gok_empty[kbuf], ((g / Cfg::GOK_NB) & 1u) ^ 1u, abort_flag, kErrBwdScores | 3))
+                  goto done;
+                if (leader) mbar_arrive_expect_tx(&gok_full[kbuf], 2 * Cfg::GOK_BYTES);
+                const uint32_t gb = mapa_shared(smem_u32(&gok_full[kbuf]), 0);
+#pragma unroll
+                for (int jj = 0; jj < Cfg::NCH; ++jj)
+#pragma unroll
+                  for (int c = 0; c < DP / 64; ++c)
+                    tma_load_2d_pair(smem + Cfg::SMEM_GOK + kbuf * Cfg::GOK_BYTES + jj * Cfg::GOK_CH + c * Cfg::GOK_CBOX,
+                                     &tm_gok, gb, c * 64,
+                                     it * BN + jj * Cfg::DPC + static_cast<int>(rank) * (Cfg::DPC / 2));
+              }
+              // MN-major gO of the tile whose dE comes next: with single-buffered S this tile
+              // (its dE runs before the next S); otherwise the previous tile of the pair,
+              // which may belong to the previous unit
+              const bool gom_now = Cfg::kSingleS || g > 0;
+              if (gom_now) {
+                const uint32_t fill = Cfg::kSingleS ? g : g - 1u;  // one MN-major fill per tile
+                const int gom_tile = Cfg::kSingleS ? it : prev_it;
+                if (!mbar_wait(gom_empty, (fill & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+                if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+                const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+                for (int c = 0; c < Cfg::GOM_NB; ++c)
+                  tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                                   static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, gom_tile * BN);
+              }
+            }
+            if (it == it0 && kb == (Cfg::kSingleS ? kx : KB - 1)) {
+              // E of this unit.  With double-buffered S the previous unit's last dP chunks
+              // may still be issued during this tile's S loop, so E is replaced at its end.
               if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
               if (leader) mbar_arrive_expect_tx(e_full, 2 * Cfg::E_BYTES);
               const uint32_t eb = mapa_shared(smem_u32(e_full), 0);
@@ -206,46 +245,20 @@ __global__ void __launch_bounds__(256, 1)
               for (int c = 0; c < DP / 64; ++c)
                 tma_load_2d_pair(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, eb, c * 64, vrow0);
             }
-            {
-              // gO, K-major: this CTA's DPC/2 tokens of each dP chunk
-              const uint32_t kbuf = g % Cfg::GOK_NB;
-              if (!mbar_wait(&gok_empty[kbuf], ((g / Cfg::GOK_NB) & 1u) ^ 1u, abort_flag, kErrBwdScores | 3))
-                goto done;
-              if (leader) mbar_arrive_expect_tx(&gok_full[kbuf], 2 * Cfg::GOK_BYTES);
-              const uint32_t gb = mapa_shared(smem_u32(&gok_full[kbuf]), 0);
-#pragma unroll
-              for (int jj = 0; jj < Cfg::NCH; ++jj)
-#pragma unroll
-                for (int c = 0; c < DP / 64; ++c)
-                  tma_load_2d_pair(smem + Cfg::SMEM_GOK + kbuf * Cfg::GOK_BYTES + jj * Cfg::GOK_CH + c * Cfg::GOK_CBOX,
-                                   &tm_gok, gb, c * 64, it * BN + jj * Cfg::DPC + static_cast<int>(rank) * (Cfg::DPC / 2));
-            }
-            // MN-major gO: with single-buffered S the tile's dE comes before the next S, so it
-            // is loaded with this tile's K-major copy; otherwise the previous tile's, here
-            const int gom_tile = Cfg::kSingleS ? it : it - 1;
-            if (gom_tile >= it0) {
-              const uint32_t gom_use = Cfg::kSingleS ? g : g - 1u;
-              if (!mbar_wait(gom_empty, (gom_use & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
-              if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
-              const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
-#pragma unroll
-              for (int c = 0; c < Cfg::GOM_NB; ++c)
-                tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
-                                 static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, gom_tile * BN);
-            }
           }
-        }
-        if (!Cfg::kSingleS) {
-          // the unit's last tile: its MN-major gO, once the previous tile's dE has read the buffer
-          if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
-          if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
-          const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
-#pragma unroll
-          for (int c = 0; c < Cfg::GOM_NB; ++c)
-            tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
-                             static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, (it1 - 1) * BN);
+          prev_it = it;
         }
         ++uc;
+      }
+      if (!Cfg::kSingleS && g > 0) {
+        // the pair's last tile: its MN-major gO, once the previous tile's dE has read the buffer
+        if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+        if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+        const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+        for (int c = 0; c < Cfg::GOM_NB; ++c)
+          tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                           static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, prev_it * BN);
       }
     }
   } else if (warp == 1) {
@@ -263,8 +276,23 @@ __global__ void __launch_bounds__(256, 1)
       // stage-0 descriptors; a stage / K half / 16-wide K step adds (byte offset >> 4)
       const uint64_t da0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_A), 16, 1024);
       const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
-      // dP^T chunk jj of tile gt (global tile counter): E . gO_chunk^T into the dP buffer
-      auto issue_dp = [&](uint32_t gt, int jj) {
+      // S^T of tile g (global tile counter) into S buffer b: the unit's K loop
+      auto issue_s = [&](uint32_t b, uint32_t kb) {
+        const uint64_t sa = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));
+        const uint64_t sb = static_cast<uint64_t>(stage * (Cfg::B_BYTES >> 4));
+#pragma unroll
+        for (int k8 = 0; k8 < 4 * KH; ++k8)
+          umma2_ss(tmem + Cfg::S_COL + b * BN, da0 + sa + (k8 >> 2) * (Cfg::BOX >> 4) + (k8 & 3) * 2,
+                   db0 + sb + (k8 >> 2) * (Cfg::HBOX >> 4) + (k8 & 3) * 2, idS, (kb | k8) ? 1u : 0u);
+        umma2_commit_mc(&empty[stage], 3);
+        if (++stage == NS) {
+          stage = 0;
+          sphase ^= 1u;
+        }
+      };
+      // dP^T chunk jj of tile gt: E . gO_chunk^T into the dP buffer.  After the last chunk of
+      // a unit's last tile the unit's E may be replaced.
+      auto issue_dp = [&](uint32_t gt, int jj, bool unit_last) {
         const uint32_t kbuf = gt % Cfg::GOK_NB;
         const uint32_t gk = gokbase + kbuf * Cfg::GOK_BYTES + jj * Cfg::GOK_CH;
         tc_fence_after();
@@ -272,102 +300,122 @@ __global__ void __launch_bounds__(256, 1)
         for (int ks = 0; ks < DP / 16; ++ks)
           umma2_ss(tmem + Cfg::DP_COL, sdesc_sw128(ebase + (ks >> 2) * Cfg::BOX + (ks & 3) * 32, 16, 1024),
                    sdesc_sw128(gk + (ks >> 2) * Cfg::GOK_CBOX + (ks & 3) * 32, 16, 1024), idDP, ks ? 1u : 0u);
-        if (jj == Cfg::NCH - 1) umma2_commit_mc(&gok_empty[kbuf], 3);
+        if (jj == Cfg::NCH - 1) {
+          umma2_commit_mc(&gok_empty[kbuf], 3);
+          if (unit_last) umma2_commit_mc(e_empty, 3);
+        }
         umma2_commit_mc(dp_full, 3);
       };
-      for (int u = pair; u < p.units; u += npairs) {
-        const int ts = u % p.TS;
-        const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
-        const int n = it1 - it0;
-        if (n <= 0) continue;
-        int pj = Cfg::NCH;  // next dP chunk of the previous tile (NCH: none left)
-        for (int j = 0; j <= n; ++j) {
-          if (j < n) {
-            // (single-buffered S: the previous tile's dE, issued above, read P before this S)
-            const uint32_t b = Cfg::kSingleS ? 0u : (g & 1u);
+      // dE += P^T . gO of tile gt (S buffer sb), once both CTAs' gradient passes have written
+      // P; the first tile of a unit overwrites dE, after the previous unit's dE was read out.
+      auto issue_de = [&](uint32_t gt, uint32_t sb, bool unit_first, bool unit_last, uint32_t guc) -> bool {
+        if (!mbar_wait(gom_full, gt & 1u, abort_flag, kErrBwdScores | 9)) return false;
+        if (need_de) {
+          if (unit_first && guc > 0 && !mbar_wait(de_free, (guc - 1u) & 1u, abort_flag, kErrBwdScores | 9))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < BN / 16; ++ks) {
+            const uint64_t bdesc = Cfg::GOM_ROW == 64 ? sdesc_sw64(gombase + ks * 16 * 64, Cfg::GOM_BOX, 512)
+                                                      : sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BOX, 1024);
+            umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + sb * BN + ks * 8, bdesc, idDE,
+                     (unit_first && ks == 0) ? 0u : 1u);
+          }
+        }
+        umma2_commit_mc(gom_empty, 3);
+        if (need_de && unit_last) umma2_commit_mc(de_full, 3);
+        return true;
+      };
+      if constexpr (Cfg::kSingleS) {
+        // one S buffer: each tile's S, dP, gradient pass and dE before the next tile's S
+        for (int u = pair; u < p.units; u += npairs) {
+          const int ts = u % p.TS;
+          const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+          const int n = it1 - it0;
+          if (n <= 0) continue;
+          for (int j = 0; j < n; ++j, ++g) {
             for (int kb = 0; kb < KB; ++kb) {
               if (!mbar_wait(&full[stage], sphase, abort_flag, kErrBwdScores | 5)) goto done;
-              const uint64_t sa = static_cast<uint64_t>(stage * (Cfg::A_BYTES >> 4));
-              const uint64_t sb = static_cast<uint64_t>(stage * (Cfg::B_BYTES >> 4));
-#pragma unroll
-              for (int k8 = 0; k8 < 4 * KH; ++k8)
-                umma2_ss(tmem + Cfg::S_COL + b * BN, da0 + sa + (k8 >> 2) * (Cfg::BOX >> 4) + (k8 & 3) * 2,
-                         db0 + sb + (k8 >> 2) * (Cfg::HBOX >> 4) + (k8 & 3) * 2, idS, (kb | k8) ? 1u : 0u);
-              umma2_commit_mc(&empty[stage], 3);
-              if (++stage == NS) {
-                stage = 0;
-                sphase ^= 1u;
-              }
+              issue_s(0u, kb);
+            }
+            umma2_commit_mc(&s_full[0], 3);
+            if (q > 0 && !mbar_wait(dp_free, (q - 1u) & 1u, abort_flag, kErrBwdScores | 6)) goto done;
+            if (j == 0 && !mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 6)) goto done;
+            if (!mbar_wait(&gok_full[0], g & 1u, abort_flag, kErrBwdScores | 7)) goto done;
+            issue_dp(g, 0, j == n - 1);
+            ++q;
+            if (!mbar_wait(&p_ready[0], g & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+            if (!issue_de(g, 0u, j == 0, j == n - 1, uc)) goto done;
+          }
+          ++uc;
+        }
+      } else {
+        // Two S buffers: tile g's S loop runs while the gradient warps process tile g-1; the
+        // pair's tiles form one sequence across units, so a unit's last tile is finished
+        // (remaining dP chunks, dE) during the next unit's first S loop.
+        int pj = Cfg::NCH;  // next dP chunk of the previous tile (NCH: none left)
+        bool prev_first = false, prev_last = false;  // the previous tile opens / closes its unit
+        uint32_t prev_uc = 0;                        // and its unit
+        for (int u = pair; u < p.units; u += npairs) {
+          const int ts = u % p.TS;
+          const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+          const int n = it1 - it0;
+          if (n <= 0) continue;
+          for (int j = 0; j < n; ++j, ++g) {
+            const uint32_t b = g & 1u;
+            for (int kb = 0; kb < KB; ++kb) {
+              if (!mbar_wait(&full[stage], sphase, abort_flag, kErrBwdScores | 5)) goto done;
+              issue_s(b, kb);
               if constexpr (Cfg::NCH > 1) {
                 // the previous tile's next dP chunk, once its gradient passes have read the last
                 if (pj < Cfg::NCH && mbar_test(dp_free, (q - 1u) & 1u)) {
-                  issue_dp(g - 1u, pj);
+                  issue_dp(g - 1u, pj, prev_last);
                   ++pj;
                   ++q;
                 }
               }
             }
             umma2_commit_mc(&s_full[b], 3);
-          }
-          // the previous tile's remaining dP chunks
-          while (pj < Cfg::NCH) {
-            if (!mbar_wait(dp_free, (q - 1u) & 1u, abort_flag, kErrBwdScores | 13)) goto done;
-            issue_dp(g - 1u, pj);
-            ++pj;
-            ++q;
-          }
-          if (j < n) {
+            // the previous tile's remaining dP chunks
+            while (pj < Cfg::NCH) {
+              if (!mbar_wait(dp_free, (q - 1u) & 1u, abort_flag, kErrBwdScores | 13)) goto done;
+              issue_dp(g - 1u, pj, prev_last);
+              ++pj;
+              ++q;
+            }
+            const bool have_prev = g > 0;
+            if (have_prev) {
+              if (!mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+              // across a unit boundary the previous unit's dE goes first: this tile's first dP
+              // chunk waits for the new E, which the producer loads at the end of this S loop
+              if (prev_last && !issue_de(g - 1u, (g - 1u) & 1u, prev_first, true, prev_uc)) goto done;
+            }
             // this tile's first dP chunk, once both CTAs' gradient passes have read the last one
             if (q > 0 && !mbar_wait(dp_free, (q - 1u) & 1u, abort_flag, kErrBwdScores | 6)) goto done;
             if (j == 0 && !mbar_wait(e_full, uc & 1u, abort_flag, kErrBwdScores | 6)) goto done;
             if (!mbar_wait(&gok_full[g % Cfg::GOK_NB], (g / Cfg::GOK_NB) & 1u, abort_flag, kErrBwdScores | 7))
               goto done;
-            issue_dp(g, 0);
+            issue_dp(g, 0, j == n - 1);
             ++q;
             pj = 1;
-            ++g;
-            if (Cfg::kSingleS) {
-              // this tile's gradient pass, then its dE, before the next tile's S overwrites P
-              const uint32_t gg = g - 1u;
-              if (!mbar_wait(&p_ready[0], gg & 1u, abort_flag, kErrBwdScores | 8)) goto done;
-              if (!mbar_wait(gom_full, gg & 1u, abort_flag, kErrBwdScores | 9)) goto done;
-              if (need_de) {
-                const bool first = (j == 0);
-                if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
-                tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < BN / 16; ++ks)
-                  umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + ks * 8,
-                           sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BOX, 1024), idDE,
-                           (first && ks == 0) ? 0u : 1u);
-              }
-              umma2_commit_mc(gom_empty, 3);
-            }
+            if (have_prev && !prev_last && !issue_de(g - 1u, (g - 1u) & 1u, prev_first, false, prev_uc)) goto done;
+            prev_first = j == 0;
+            prev_last = j == n - 1;
+            prev_uc = uc;
           }
-          if (!Cfg::kSingleS && j > 0) {
-            // dE of the tile before the one just started (or of the unit's last tile)
-            const uint32_t gg = g - 1u - (j < n ? 1u : 0u);
-            if (!mbar_wait(&p_ready[gg & 1u], (gg >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
-            if (!mbar_wait(gom_full, gg & 1u, abort_flag, kErrBwdScores | 9)) goto done;
-            if (need_de) {
-              const bool first = (j == 1);
-              if (first && uc > 0 && !mbar_wait(de_free, (uc - 1u) & 1u, abort_flag, kErrBwdScores | 9)) goto done;
-              tc_fence_after();
-#pragma unroll
-              for (int ks = 0; ks < BN / 16; ++ks) {
-                const uint64_t bdesc = Cfg::GOM_ROW == 64
-                                           ? sdesc_sw64(gombase + ks * 16 * 64, Cfg::GOM_BOX, 512)
-                                           : sdesc_sw128(gombase + ks * 16 * 128, Cfg::GOM_BOX, 1024);
-                umma2_ts(tmem + Cfg::DE_COL, tmem + Cfg::S_COL + (gg & 1u) * BN + ks * 8, bdesc, idDE,
-                         (first && ks == 0) ? 0u : 1u);
-              }
-            }
-            umma2_commit_mc(gom_empty, 3);
-          }
+          ++uc;
         }
-        umma2_commit_mc(e_empty, 3);
-        if (need_de) umma2_commit_mc(de_full, 3);
-        ++uc;
+        if (g > 0) {
+          // the pair's last tile
+          while (pj < Cfg::NCH) {
+            if (!mbar_wait(dp_free, (q - 1u) & 1u, abort_flag, kErrBwdScores | 13)) goto done;
+            issue_dp(g - 1u, pj, prev_last);
+            ++pj;
+            ++q;
+          }
+          if (!mbar_wait(&p_ready[(g - 1u) & 1u], ((g - 1u) >> 1) & 1u, abort_flag, kErrBwdScores | 8)) goto done;
+          if (!issue_de(g - 1u, (g - 1u) & 1u, prev_first, true, prev_uc)) goto done;
+        }
       }
     }
   } else if (warp >= 4) {
