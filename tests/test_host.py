@@ -150,3 +150,30 @@ def test_selftest_limits_are_checked_on_the_host():
     assert lib.swvr_selftest_wait_timeout(10, None) == nat.ERR_INVALID_ARGUMENT
     assert lib.swvr_selftest_wait_timeout(20_000_000_000, None) == nat.ERR_INVALID_ARGUMENT
     assert "limit_ns" in nat.last_error()
+
+
+def test_backward_token_tile_choice_and_override(monkeypatch):
+    """The score kernel's token tile sets dS's token pitch and so the backward workspace:
+    192-token tiles by default for D <= 64 with hidden >= 1024, 128 otherwise;
+    SWVR_BWD_TOKEN_TILE=128|192 overrides where that tile exists (192 needs D <= 64)."""
+    lib = nat.lib()
+    g = nat.Grads()
+    g.grad_h, g.grad_W, g.grad_E = 1 << 20, 1 << 20, 1 << 20
+
+    def ws(tile, **kw):
+        if tile is None:
+            monkeypatch.delenv("SWVR_BWD_TOKEN_TILE", raising=False)
+        else:
+            monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", tile)
+        n = ctypes.c_size_t(0)
+        assert lib.swvr_bwd_workspace_size(_problem(**kw), g, ctypes.byref(n)) == nat.OK
+        return n.value
+
+    long_k = dict(N=16384, K=2560, V=19008, D=64)
+    # dS is [chunk rows, 86 x 192 = 16512 tokens] against 128 x 128 = 16384, and the dE / db
+    # partial slots follow the token splits of each plan
+    assert ws(None, **long_k) == ws("192", **long_k) != ws("128", **long_k)
+    short_k = dict(N=16384, K=512, V=19008, D=64)
+    assert ws(None, **short_k) == ws("128", **short_k) != ws("192", **short_k)
+    wide_d = dict(N=16384, K=2560, V=19008, D=128)
+    assert ws(None, **wide_d) == ws("128", **wide_d) == ws("192", **wide_d)
