@@ -151,7 +151,9 @@ typedef struct swvr_grads {
  * Backward.  Replaces swvr::chunked_bwd (swvr/chunked.py:170-178 -> _backward, 108-151):
  * recomputes the scores per vocabulary tile and writes dh, dW, dE and db.  dW, dE and db are
  * deterministic (fixed-order reductions, no atomics); dh is accumulated in fp32 across
- * chunks in chunk order.
+ * chunks in chunk order.  The workspace size depends on the score kernel's token tile, which
+ * the environment variable SWVR_BWD_TOKEN_TILE (128 or 192) can override: keep it unchanged
+ * between the size query and the call.
  */
 int swvr_bwd_workspace_size(const swvr_problem* p, const swvr_grads* g, size_t* bytes);
 int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t workspace_bytes, void* stream);
