@@ -158,3 +158,77 @@ def test_replicate_from_host(tmp_path, world):
         np.testing.assert_array_equal(z["h"], z["ref_h"])
         np.testing.assert_array_equal(z["w"], z["ref_w"])
         assert bool(z["same"])
+
+
+# ---------------------------------------------------------------------- DDP x vocabulary-parallel grid
+class _GridModel(torch.nn.Module):
+    """A trunk (replicated) feeding a readout whose head / embedding rows are this rank's
+    vocabulary shard; the loss (plain torch on O, LSE) is the same on the ranks of a shard group."""
+
+    def __init__(self, trunk_w, trunk_b, Ws, Es, bs, tp_group):
+        super().__init__()
+        self.trunk = torch.nn.Linear(trunk_w.shape[1], trunk_w.shape[0], dtype=torch.float64)
+        with torch.no_grad():
+            self.trunk.weight.copy_(trunk_w)
+            self.trunk.bias.copy_(trunk_b)
+        self.Ws, self.Es, self.bs = (torch.nn.Parameter(x.clone()) for x in (Ws, Es, bs))
+        self.tp_group = tp_group
+
+    def forward(self, x, t):
+        from swvr_b200 import vocab_parallel as vp
+        h = torch.tanh(self.trunk(x))
+        O, lse = vp.softmax_readout_vocab_parallel(h, self.Ws, self.Es, self.bs, logit_scale=0.5, chunk_size=8,
+                                                   group=self.tp_group)
+        return ((O - t) ** 2).mean() + 1e-3 * (lse ** 2).mean()
+
+
+def _grid_inputs(N=6, K=12, V=41, D=5):
+    g = torch.Generator().manual_seed(3)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)
+    return dict(x=r(2 * N, K), t=r(2 * N, D), tw=0.3 * r(K, K), tb=0.1 * r(K), W=r(V, K), E=r(V, D), b=r(V), N=N)
+
+
+def _grid_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from swvr_b200 import vocab_parallel as vp
+    vp.set_backend(OracleBackend)
+    # 2 x 2 grid: data replica dp = rank // 2, vocabulary shard tp = rank % 2; every rank
+    # creates every group, in the same order
+    tp_groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
+    dp_groups = [dist.new_group([0, 2]), dist.new_group([1, 3])]
+    dp, tp = rank // 2, rank % 2
+    z = _grid_inputs()
+    v0, v1 = vp.shard_range(z["W"].shape[0], 2, tp)
+    model = _GridModel(z["tw"], z["tb"], z["W"][v0:v1], z["E"][v0:v1], z["b"][v0:v1], tp_groups[dp])
+    ddp = torch.nn.parallel.DistributedDataParallel(model, process_group=dp_groups[tp])
+    rows = slice(dp * z["N"], (dp + 1) * z["N"])
+    ddp(z["x"][rows], z["t"][rows]).backward()
+    m = ddp.module
+    np.savez(os.path.join(out_dir, f"grid{rank}.npz"), tw=m.trunk.weight.grad.numpy(), tb=m.trunk.bias.grad.numpy(),
+             gW=m.Ws.grad.numpy(), gE=m.Es.grad.numpy(), gb=m.bs.grad.numpy(), v0=v0, v1=v1)
+    dist.destroy_process_group()
+
+
+def test_ddp_over_vocab_parallel_grid(tmp_path):
+    """DDP over the data-parallel group composed with the vocabulary-parallel readout over the
+    shard group (2 x 2 ranks): every rank's gradients equal the full-batch, unsharded model's
+    (trunk on every rank, head / embedding / bias rows on their shard's ranks)."""
+    mp.spawn(_grid_worker, args=(4, _free_port(), str(tmp_path)), nprocs=4, join=True)
+    z = _grid_inputs()
+    trunk = torch.nn.Linear(z["tw"].shape[1], z["tw"].shape[0], dtype=torch.float64)
+    with torch.no_grad():
+        trunk.weight.copy_(z["tw"])
+        trunk.bias.copy_(z["tb"])
+    W, E, b = (z[k].clone().requires_grad_(True) for k in ("W", "E", "b"))
+    S = 0.5 * torch.tanh(trunk(z["x"])) @ W.t() + b
+    O, lse = torch.softmax(S, dim=1) @ E, torch.logsumexp(S, dim=1)
+    (((O - z["t"]) ** 2).mean() + 1e-3 * (lse ** 2).mean()).backward()
+    for r in range(4):
+        o = np.load(tmp_path / f"grid{r}.npz")
+        v0, v1 = int(o["v0"]), int(o["v1"])
+        np.testing.assert_allclose(o["tw"], trunk.weight.grad.numpy(), rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(o["tb"], trunk.bias.grad.numpy(), rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(o["gW"], W.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(o["gE"], E.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
+        np.testing.assert_allclose(o["gb"], b.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
