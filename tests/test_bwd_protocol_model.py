@@ -21,33 +21,10 @@ import random
 
 import pytest
 
-
-class Bar:
-    def __init__(self, name, count):
-        self.name, self.count, self.pending, self.done = name, count, count, 0
-
-    def arrive(self, phase):
-        assert phase == self.done, (self.name, "arrival for phase", phase, "current", self.done)
-        self.pending -= 1
-        if self.pending == 0:
-            self.done += 1
-            self.pending = self.count
-
-    def passes(self, parity):
-        return (self.done & 1) != parity
-
-    def test(self, parity):
-        return self.passes(parity)
-
-
-class Wait:
-    def __init__(self, bar, parity, m):
-        assert parity == (m & 1), (bar.name, parity, m)
-        self.bar, self.parity, self.m = bar, parity, m
+from tests.protocol_model import Bar, Wait, schedule
 
 
 def run(cfg, seed, skip_dp_free_test=False):
-    rnd = random.Random(seed)
     NS, KB, NCH, single, need_de, units = cfg["NS"], cfg["KB"], cfg["NCH"], cfg["single"], cfg["need_de"], cfg["units"]
     GOK_NB = 2 if NCH > 1 else 1
     kx = min(NS, KB - 1)
@@ -258,8 +235,7 @@ def run(cfg, seed, skip_dp_free_test=False):
             yield Wait(p_ready[(g - 1) & 1], ((g - 1) >> 1) & 1, (g - 1) >> 1)
             yield from issue_de(g - 1, prev_first, True, prev_uc)
 
-    def pipe_step():
-        op = st["pipe"].pop(0)
+    def pipe_step(op):
         kind = op[0]
         if kind == "commit":
             for bar in op[1]:
@@ -334,43 +310,7 @@ def run(cfg, seed, skip_dp_free_test=False):
             uc += 1
 
     roles = {"p0": producer(0), "p1": producer(1), "mma": issuer(), "g0": grad(0), "g1": grad(1)}
-    waiting = {k: None for k in roles}
-    finished = set()
-    steps = 0
-    while True:
-        steps += 1
-        assert steps < 10_000_000
-        runnable = []
-        for k in roles:
-            if k in finished:
-                continue
-            w = waiting[k]
-            if w is None or w.bar.passes(w.parity):
-                runnable.append(k)
-        if st["pipe"]:
-            runnable.append("pipe")
-        if not runnable:
-            if len(finished) == len(roles):
-                break
-            raise AssertionError("deadlock: " + ", ".join(
-                f"{k} waits {w.bar.name} m={w.m} done={w.bar.done}" for k, w in waiting.items() if k not in finished))
-        k = rnd.choice(runnable)
-        if k == "pipe":
-            pipe_step()
-            continue
-        w = waiting[k]
-        if w is not None:
-            assert w.bar.done == w.m + 1, (k, w.bar.name, "passes at", w.bar.done, "meant", w.m)
-            waiting[k] = None
-        try:
-            nw = next(roles[k])
-            if isinstance(nw, Wait):
-                assert nw.bar.done <= nw.m + 1, (k, nw.bar.name, "overrun", nw.bar.done, nw.m)
-            waiting[k] = nw
-        except StopIteration:
-            finished.add(k)
-    assert not st["pipe"]
-    return steps
+    schedule(roles, st["pipe"], pipe_step, seed)
 
 
 def _configs(n, seed=1):
