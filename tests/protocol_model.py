@@ -38,6 +38,21 @@ class Wait:
         self.bar, self.parity, self.m = bar, parity, m
 
 
+class Until:
+    """A wait on something other than an mbarrier (e.g. a bulk-copy group count): passes when
+    ``predicate()`` holds."""
+
+    def __init__(self, predicate, name):
+        self.predicate, self.name = predicate, name
+
+    def passes(self):
+        return self.predicate()
+
+
+def _ready(w):
+    return w is None or (w.passes() if isinstance(w, Until) else w.bar.passes(w.parity))
+
+
 def schedule(roles, pipe, pipe_step, seed, max_steps=10_000_000):
     """Run generator ``roles`` (name -> generator) and the FIFO ``pipe`` (executed by
     ``pipe_step``) in a seeded random order until every role finishes and the pipe is empty."""
@@ -45,23 +60,23 @@ def schedule(roles, pipe, pipe_step, seed, max_steps=10_000_000):
     waiting = {k: None for k in roles}
     finished = set()
     for _ in range(max_steps):
-        runnable = [k for k in roles if k not in finished and (waiting[k] is None or
-                                                                waiting[k].bar.passes(waiting[k].parity))]
+        runnable = [k for k in roles if k not in finished and _ready(waiting[k])]
         if pipe:
             runnable.append(None)
         if not runnable:
             if len(finished) == len(roles):
                 return
             raise AssertionError("deadlock: " + ", ".join(
-                f"{k} waits {w.bar.name} m={w.m} done={w.bar.done}" for k, w in waiting.items() if k not in finished))
+                (f"{k} waits {w.name}" if isinstance(w, Until) else f"{k} waits {w.bar.name} m={w.m} done={w.bar.done}")
+                for k, w in waiting.items() if k not in finished))
         k = rnd.choice(runnable)
         if k is None:
             pipe_step(pipe.pop(0))
             continue
         w = waiting[k]
-        if w is not None:
+        if isinstance(w, Wait):
             assert w.bar.done == w.m + 1, (k, w.bar.name, "passes at", w.bar.done, "meant", w.m)
-            waiting[k] = None
+        waiting[k] = None
         try:
             nw = next(roles[k])
             if isinstance(nw, Wait):
