@@ -177,3 +177,27 @@ def test_backward_token_tile_choice_and_override(monkeypatch):
     assert ws(None, **short_k) == ws("128", **short_k) != ws("192", **short_k)
     wide_d = dict(N=16384, K=2560, V=19008, D=128)
     assert ws(None, **wide_d) == ws("128", **wide_d) == ws("192", **wide_d)
+
+
+def test_forward_and_backward_reject_bad_arguments_before_any_launch():
+    """swvr_fwd / swvr_bwd check their arguments on the host before touching the device (this
+    container has none): NULL grads or backward inputs, a workspace smaller than the size
+    query's, a grad_W dtype other than the compute dtype or fp32, a misaligned grad_W."""
+    lib = nat.lib()
+    p = _problem()
+    buf, big = 1 << 20, 1 << 40
+    assert lib.swvr_fwd(p, buf, buf, buf, 16, None) == nat.ERR_WORKSPACE
+    assert lib.swvr_bwd(p, None, None, 0, None) == nat.ERR_INVALID_ARGUMENT
+    g = nat.Grads()
+    assert lib.swvr_bwd(p, g, None, 0, None) == nat.ERR_INVALID_ARGUMENT  # NULL O / lse / grad_O / grad_lse
+    g.O = g.lse = g.grad_O = g.grad_lse = buf
+    g.grad_W, g.grad_W_dtype, g.ld_grad_W = buf, nat.BF16, p.hidden
+    assert lib.swvr_bwd(p, g, buf, 16, None) == nat.ERR_WORKSPACE
+    g.grad_W_dtype = nat.F16
+    assert lib.swvr_bwd(p, g, buf, big, None) == nat.ERR_UNSUPPORTED
+    assert "grad_W" in nat.last_error()
+    g.grad_W_dtype, g.grad_W = nat.BF16, buf + 8
+    assert lib.swvr_bwd(p, g, buf, big, None) == nat.ERR_UNSUPPORTED
+    assert "aligned" in nat.last_error()
+    with pytest.raises(RuntimeError):
+        nat.check(nat.ERR_UNSUPPORTED, "swvr_bwd")
