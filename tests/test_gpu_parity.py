@@ -366,8 +366,12 @@ def test_masked_vocab_with_neg_inf_bias(dtype):
 
 
 @pytest.mark.parametrize("frozen", ["h", "W", "E", "b", "WE", "hW"])
-@pytest.mark.parametrize("dtype", [f64, torch.bfloat16])
-def test_frozen_inputs(frozen, dtype):
+@pytest.mark.parametrize("dtype,tile", [(f64, None), (torch.bfloat16, "128"), (torch.bfloat16, "192")])
+def test_frozen_inputs(monkeypatch, frozen, dtype, tile):
+    """Frozen inputs skip their work (no dE / db partials, no dS when neither h nor W needs a
+    gradient); bf16 runs both score-tile widths."""
+    if tile is not None:
+        monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", tile)
     h, W, E, b = make_cpu(K=16, V=300, D=8, dtype=dtype)
     names = dict(h=h, W=W, E=E, b=b)
     for k in frozen:
