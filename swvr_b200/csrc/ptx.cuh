@@ -403,7 +403,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-// Multiply both 16-bit halves of a packed pair by a power of two (exact barring underflow).
+// Multiply both 16-bit halves of a packed pair by alpha, rounding the products back to 16 bits.
 template <bool kBF16>
 __device__ __forceinline__ uint32_t scale2(uint32_t v, float alpha) {
   float lo, hi;
