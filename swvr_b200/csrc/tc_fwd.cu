@@ -275,8 +275,8 @@ __global__ void __launch_bounds__(256, 1)
             const float newref = emerg ? cm : ref;
             const float alpha = newref == ref ? 1.f : ex2(ref - newref);
             if (c > 0) {
-              // rescale this tile's P chunks already written (16-bit pairs; one more rounding of
-              // values that the jump of more than 2^kEmergency has just made negligible)
+              // rescale this tile's P chunks already written (16-bit pairs): their products are
+              // rounded to 16 bits again, so those P values carry a second rounding
 #pragma unroll 1
               for (int cc = 0; cc < c; ++cc) {
                 uint32_t pk[16];
