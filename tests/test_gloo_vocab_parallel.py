@@ -58,12 +58,12 @@ def _inputs(N=7, K=12, V=41, D=5):
     return h, W, E, b, gO, glse
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, V):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     from swvr_b200 import vocab_parallel as vp
     vp.set_backend(OracleBackend)
-    h, W, E, b, gO, glse = _inputs()
+    h, W, E, b, gO, glse = _inputs(V=V)
     v0, v1 = vp.shard_range(W.shape[0], world, rank)
     h = h.clone().requires_grad_(True)
     Ws, Es, bs = (x[v0:v1].clone().requires_grad_(True) for x in (W, E, b))
@@ -74,10 +74,10 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_vocab_parallel_matches_unsharded(tmp_path, world):
-    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
-    h, W, E, b, gO, glse = (x.numpy() for x in _inputs())
+@pytest.mark.parametrize("world,V", [(2, 41), (3, 41), (3, 2)])  # V=2 on 3 ranks: rank 0's shard is empty
+def test_vocab_parallel_matches_unsharded(tmp_path, world, V):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), V), nprocs=world, join=True)
+    h, W, E, b, gO, glse = (x.numpy() for x in _inputs(V=V))
     O_ref, lse_ref = orc.softmax_readout_reference(h, W, E, b, 0.5)
     gh, gW, gE, gb = orc.readout_grads(h, W, E, b, gO, glse, 0.5)
     outs = [dict(np.load(tmp_path / f"rank{r}.npz")) for r in range(world)]
