@@ -30,13 +30,15 @@ def _check(h, W, E, bias):
 
 
 def softmax_readout(h, W, E, bias=None, *, logit_scale=1.0, chunk_size=None):
-    """Return ``(O, LSE)`` for ``S = logit_scale * h @ W.T + bias`` (swvr/api.py:25-41).
+    """The softmax-weighted embedding readout (swvr/api.py:25-41).
 
-    ``O = softmax(S) @ E`` has shape ``[..., D]`` and ``LSE = logsumexp(S)`` has shape ``[...]``,
-    both in fp32 (fp64 for fp64 inputs). ``h`` is ``[..., K]``, ``W`` is ``[V, K]``, ``E`` is
-    ``[V, D]`` and ``bias`` is ``[V]``. Gradients flow to every input that requires them.
-    The ``[..., V]`` scores are never materialised; ``chunk_size`` (default 8192, or env
-    ``SWVR_CHUNK``) bounds the vocabulary rows whose score gradients the backward stages.
+    Scores are ``S = logit_scale * h @ W.T + bias`` over a vocabulary of V rows (W ``[V, K]``,
+    optional bias ``[V]``); the result is the pair ``O = softmax(S) @ E`` (E ``[V, D]``) and
+    ``LSE = logsumexp(S)``.  h may carry any leading dims ``[..., K]``: O comes back as
+    ``[..., D]`` and LSE as ``[...]``, in fp32 (fp64 when the inputs are fp64), differentiable
+    in every input that requires grad.  The kernels stream the vocabulary in tiles, so no
+    ``[..., V]`` tensor is ever allocated; ``chunk_size`` (default 8192, env ``SWVR_CHUNK``)
+    caps how many vocabulary rows of score gradients the backward keeps at once.
     """
     _check(h, W, E, bias)
     lead = h.shape[:-1]
@@ -50,12 +52,14 @@ def softmax_readout(h, W, E, bias=None, *, logit_scale=1.0, chunk_size=None):
 
 def softmax_readout_mse(h, W, E, target, bias=None, *, weight=None, reduction="mean",
                         z_loss_weight=0.0, logit_scale=1.0, chunk_size=None):
-    """MSE between ``softmax(S) @ E`` and ``target`` (``[..., D]``), plus an optional z-loss.
+    """Mean-squared error of the readout ``O`` against ``target`` (swvr/api.py:44-66).
 
-    swvr/api.py:44-66. The per-token loss is ``mean_d (O - target)^2 + z_loss_weight * LSE^2``.
-    ``weight`` (shape ``[...]``) scales each token's loss, and 0 masks it out.
-    ``reduction="mean"`` divides by ``weight.sum()`` when a weight is given, else by the token
-    count. ``"sum"`` and ``"none"`` are also accepted.
+    For each token the loss is the mean over the D embedding columns of ``(O - target)^2``,
+    plus ``z_loss_weight * LSE^2`` when that weight is non-zero; an optional per-token
+    ``weight`` (h's leading shape) multiplies it, so a zero weight drops the token.
+    ``reduction`` is ``"mean"`` (sum over tokens divided by the sum of the weights, or by the
+    token count without weights), ``"sum"`` or ``"none"`` (the per-token losses).  The
+    epilogue and its gradient (also to ``target`` and ``weight``) run as one CUDA kernel pair.
     """
     if reduction not in ("none", "sum", "mean"):
         raise ValueError(f"unknown reduction {reduction!r}")
@@ -70,11 +74,13 @@ def _weight_of(x):
 
 
 class SoftmaxReadoutMSE(nn.Module):
-    """Loss module around an existing LM head and embedding table (swvr/api.py:69-93).
+    """``softmax_readout_mse`` as an ``nn.Module`` bound to a model's head and codebook
+    (swvr/api.py:69-93).
 
-    ``head`` is an ``nn.Linear(K, V)`` (its bias is used if present) or a ``[V, K]`` tensor;
-    ``embedding`` is an ``nn.Embedding(V, D)`` or a ``[V, D]`` tensor. The module keeps
-    references, not copies, so weight tying and optimizer state stay intact.
+    ``head`` may be an ``nn.Linear(K, V)`` (whose bias, if any, becomes the score bias) or a
+    plain ``[V, K]`` weight; ``embedding`` an ``nn.Embedding(V, D)`` or a ``[V, D]`` table.
+    The module stores the objects it is given, never copies, so tied weights and the
+    optimizer's view of the parameters are unaffected.
     """
 
     def __init__(self, head, embedding, *, z_loss_weight=0.0, logit_scale=1.0,

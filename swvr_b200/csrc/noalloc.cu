@@ -16,8 +16,9 @@
 //
 // Host code never dereferences g_fwd_scratch: in host code its name is only a stand-in.
 // The first call on each device, with that device current, looks up the array's device
-// address with cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture.  Every call on a device shares the one array and leaves its last contents
+// address with cudaGetSymbolAddress and caches it with the current context (a new context on
+// that device, e.g. after cudaDeviceReset, is looked up again); make that first call before
+// any stream capture.  Every call on a device shares the one array and leaves its last contents
 // there; each call writes every slot it later reads, so nothing needs clearing.  Calls
 // whose work overlaps on the GPU (different streams, or different host threads without
 // ordering) race on the array and must be serialised by the caller.
@@ -35,20 +36,47 @@ static __device__ __align__(256) unsigned char g_fwd_scratch[kFwdScratchBytes];
 
 constexpr int kMaxDevices = 64;
 static std::mutex g_scratch_mu;
+// Per device ordinal: the context the address was looked up in, and the address.  A new
+// context on the same ordinal (after cudaDeviceReset, or a host that destroys and recreates
+// its primary context) gets a fresh lookup instead of a stale address.
+static CUcontext g_scratch_ctx[kMaxDevices] = {};
 static void* g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of g_fwd_scratch on the current device (looked up once per device).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+static CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
+
+// Device address of g_fwd_scratch on the current device, looked up once per device and
+// context (cudaGetSymbolAddress also makes the device's primary context current if no
+// context is).
 static int fwd_scratch_address(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(SWVR_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(SWVR_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  CtxGetCurrentFn get_ctx = ctx_get_current();
+  if (!get_ctx) return fail(SWVR_ERR_CUDA, "cuCtxGetCurrent is not available from the driver");
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return fail(SWVR_ERR_CUDA, "cuCtxGetCurrent failed");
+  if (!g_scratch_ptr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_fwd_scratch);
     if (e != cudaSuccess || !ptr)
       return fail(SWVR_ERR_CUDA, "cudaGetSymbolAddress(g_fwd_scratch) failed: %s", cudaGetErrorString(e));
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return fail(SWVR_ERR_CUDA, "no current CUDA context");
+    g_scratch_ctx[dev] = ctx;
     g_scratch_ptr[dev] = ptr;
   }
   *out = g_scratch_ptr[dev];

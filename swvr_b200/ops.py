@@ -21,6 +21,7 @@ import torch
 from . import _native as nat
 
 DEFAULT_CHUNK = 8192
+LOG2E = 1.4426950408889634
 
 
 def acc_dtype(cdt: torch.dtype) -> torch.dtype:
@@ -192,6 +193,42 @@ def _forward_param_cast(h, W, E, bias, logit_scale, chunk, cdt, O, lse, dev):
     return O, lse
 
 
+def _forward_state(h, W, E, bias, logit_scale, chunk, cdt):
+    """The un-normalised online-softmax state ``(m2, l, acc)`` of one vocabulary shard (for the
+    vocabulary-parallel merge): ``m2`` the row maximum of ``S * log2(e)``, ``l`` the sum of
+    ``2^(S log2 e - m2)`` and ``acc`` those weights times the rows of E.  Frozen shapes, wide
+    embeddings (the SIMT engine) and autocast over fp32 parameters go through the same
+    engine choice as the single-GPU forward; with per-chunk parameter casts the state is
+    rebuilt from the shard's normalised result as ``(LSE log2 e, 1, O)``, which merges the same."""
+    dev = _require_cuda(h, W, E, bias)
+    adt = acc_dtype(cdt)
+    N, V, D = h.shape[0], W.shape[0], E.shape[1]
+    m2 = torch.empty(N, dtype=adt, device=dev)
+    l = torch.empty(N, dtype=adt, device=dev)
+    acc = torch.empty(N, D, dtype=adt, device=dev)
+    if N == 0:
+        return m2, l, acc
+    if V == 0:
+        return m2.fill_(float("-inf")), l.zero_(), acc.zero_()
+    edt = _engine_dtype(cdt, D)
+    if _param_cast_chunks(W, E, edt):
+        O, lse = _forward_param_cast(h, W, E, bias, logit_scale, chunk, edt, acc, l, dev)
+        torch.mul(lse, LOG2E, out=m2)
+        dead = torch.isneginf(m2)  # every score -inf: an empty state, not 1 x NaN
+        l.fill_(1.0).masked_fill_(dead, 0.0)
+        return m2, l, O.masked_fill_(dead[:, None], 0.0)
+    hc, Wc, Ec, b = _prepare(h, W, E, bias, edt)
+    p = _problem(hc, Wc, Ec, b, logit_scale, chunk, edt)
+    lib = nat.lib()
+    nbytes = nat.c_size_t(0)
+    with torch.cuda.device(dev):
+        nat.check(lib.swvr_fwd_workspace_size(p, nat.ctypes.byref(nbytes)), "swvr_fwd_workspace_size")
+        ws = _workspace(nbytes.value, dev)
+        nat.check(lib.swvr_fwd_partial(p, m2.data_ptr(), l.data_ptr(), acc.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       nat.stream_ptr(dev)), "swvr_fwd_partial")
+    return m2, l, acc
+
+
 def _grad_buffer(x: torch.Tensor, cdt: torch.dtype, tc: bool) -> Tuple[torch.Tensor, torch.Tensor]:
     """(buffer the library writes, tensor returned to autograd) for a parameter's gradient."""
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
@@ -201,22 +238,30 @@ def _grad_buffer(x: torch.Tensor, cdt: torch.dtype, tc: bool) -> Tuple[torch.Ten
     return out, out
 
 
-def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b):
+def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b,
+              dh_partial=False):
+    """Gradients of one readout.  With ``dh_partial`` the first result is dh un-cast, in the
+    accumulation dtype (a vocabulary shard's contribution, summed across shards by the caller)
+    instead of dh in h's dtype."""
     dev = _require_cuda(h, W, E, bias, gO, glse, O, lse)
     adt = O.dtype
     N, K, V, D = h.shape[0], h.shape[1], W.shape[0], E.shape[1]
     cdt = _engine_dtype(cdt, D)
     tc = _tensor_core(cdt)
     need_b = need_b and bias is not None
-    gh = torch.empty(h.shape, dtype=h.dtype, device=dev) if need_h else None
+    if dh_partial:
+        gh = torch.zeros(N, K, dtype=adt, device=dev) if need_h else None
+    else:
+        gh = torch.empty(h.shape, dtype=h.dtype, device=dev) if need_h else None
     gW_buf, gW = _grad_buffer(W, cdt, tc) if need_W else (None, None)
     gE = torch.empty(E.shape, dtype=E.dtype, device=dev) if need_E else None
     gb = torch.empty(bias.shape, dtype=bias.dtype, device=dev) if need_b else None
     if not (need_h or need_W or need_E or need_b):
         return gh, gW, gE, gb
-    if V == 0:
-        if gh is not None:
-            gh.zero_()
+    if V == 0 or N == 0:
+        for x in (gh, gW, gE, gb):
+            if x is not None:
+                x.zero_()
         return gh, gW, gE, gb
     if _param_cast_chunks(W, E, cdt):
         return _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb,
@@ -226,7 +271,7 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
     padded_k = K8 != K
     gh_buf = gh
     if need_h and padded_k:
-        gh_buf = torch.empty(N, K8, dtype=h.dtype, device=dev)
+        gh_buf = torch.zeros(N, K8, dtype=gh.dtype, device=dev)
     if need_W and padded_k:
         gW_buf = torch.empty(V, K8, dtype=gW_buf.dtype, device=dev)
     p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
@@ -235,7 +280,10 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
     glse = glse.to(adt).contiguous()
     g.grad_O, g.grad_lse, g.O, g.lse = gO.data_ptr(), glse.data_ptr(), O.data_ptr(), lse.data_ptr()
     if gh_buf is not None:
-        g.grad_h, g.grad_h_dtype = gh_buf.data_ptr(), nat.dtype_code(gh_buf.dtype)
+        if dh_partial:
+            g.grad_h_acc = gh_buf.data_ptr()
+        else:
+            g.grad_h, g.grad_h_dtype = gh_buf.data_ptr(), nat.dtype_code(gh_buf.dtype)
     if gW_buf is not None:
         g.grad_W, g.grad_W_dtype, g.ld_grad_W = gW_buf.data_ptr(), nat.dtype_code(gW_buf.dtype), gW_buf.shape[1]
     if gE is not None:
@@ -258,7 +306,8 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
 def _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb, dev):
     """The backward over vocabulary chunks whose W / E rows are cast to ``cdt`` one chunk at a
     time: one ``swvr_bwd`` per chunk writes that chunk's rows of dW, dE, db and adds its dh
-    into one fp32 accumulator (``accumulate_grad_h``), which is cast once at the end."""
+    into one fp32 accumulator (``accumulate_grad_h``), which is copied into ``gh`` at the end
+    (cast to h's dtype, or kept fp32 when ``gh`` is an fp32 partial)."""
     N, K = h.shape
     hc = _prepare_k(h, cdt)
     K8 = hc.shape[1]
@@ -294,8 +343,9 @@ def _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cd
     return gh, gW, gE, gb
 
 
-# The forward and backward are opaque custom ops, so torch.compile cannot see into (and so
-# cannot reorder or materialise) the vocabulary loop; fake impls provide the shapes.
+# The readout is a pair of opaque custom ops: torch.compile traces through neither (the fake
+# impls below give it output shapes), so the vocabulary loop inside the library is never
+# unrolled into [N, V]-sized graph nodes.
 
 @torch.library.custom_op("swvr_b200::fwd", mutates_args=())
 def _fwd_op(h: torch.Tensor, W: torch.Tensor, E: torch.Tensor, bias: Optional[torch.Tensor],
@@ -309,39 +359,53 @@ def _(h, W, E, bias, logit_scale, chunk, cdt):
     return h.new_empty(h.shape[0], E.shape[1], dtype=adt), h.new_empty(h.shape[0], dtype=adt)
 
 
+def _no_grad_marker(like: torch.Tensor) -> torch.Tensor:
+    """A custom op's tensor-list result has no None: a zero-element tensor marks an input whose
+    gradient was not asked for."""
+    return like.new_empty(0)
+
+
 @torch.library.custom_op("swvr_b200::bwd", mutates_args=())
 def _bwd_op(gO: torch.Tensor, glse: torch.Tensor, h: torch.Tensor, W: torch.Tensor, E: torch.Tensor,
             bias: Optional[torch.Tensor], O: torch.Tensor, lse: torch.Tensor, logit_scale: float, chunk: int,
             cdt: torch.dtype, need_h: bool, need_W: bool, need_E: bool, need_b: bool) -> List[torch.Tensor]:
     grads = _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b)
-    # custom ops cannot return None; an empty tensor stands for "no gradient"
-    return [gr if gr is not None else h.new_empty(0) for gr in grads]
+    return [x if x is not None else _no_grad_marker(h) for x in grads]
 
 
 @_bwd_op.register_fake
 def _(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b):
-    like = [(need_h, h), (need_W, W), (need_E, E), (need_b and bias is not None, bias)]
-    return [torch.empty_like(x) if need else h.new_empty(0) for need, x in like]
+    out = []
+    for wanted, param in ((need_h, h), (need_W, W), (need_E, E), (need_b and bias is not None, bias)):
+        out.append(torch.empty_like(param) if wanted else _no_grad_marker(h))
+    return out
 
 
-def _setup_context(ctx, inputs, output):
+def _save_readout(ctx, inputs, output):
+    """Autograd keeps the operands and (O, LSE): the backward recomputes the scores from them."""
     h, W, E, bias, logit_scale, chunk, cdt = inputs
-    O, lse = output
-    ctx.save_for_backward(h, W, E, bias, O, lse)
-    ctx.args = (logit_scale, chunk, cdt)
+    ctx.save_for_backward(h, W, E, bias, *output)
+    ctx.consts = (logit_scale, chunk, cdt)
 
 
-def _autograd_backward(ctx, gO, glse):
+def _wanted_grads(ctx, bias) -> List[bool]:
+    """Which of h, W, E, bias need a gradient (bias only when there is one)."""
+    want = [bool(x) for x in ctx.needs_input_grad[:4]]
+    want[3] = want[3] and bias is not None
+    return want
+
+
+def _readout_backward(ctx, gO, glse):
     h, W, E, bias, O, lse = ctx.saved_tensors
-    needs = [bool(n) for n in ctx.needs_input_grad[:4]]
-    needs[3] = needs[3] and bias is not None
-    gO = gO if gO is not None else torch.zeros_like(O)
-    glse = glse if glse is not None else torch.zeros_like(lse)
-    grads = _bwd_op(gO, glse, h, W, E, bias, O, lse, *ctx.args, *needs)
-    return (*[gr if need else None for gr, need in zip(grads, needs)], None, None, None)
+    want = _wanted_grads(ctx, bias)
+    # an output that did not reach the loss has no incoming gradient: it contributes zero
+    gO = torch.zeros_like(O) if gO is None else gO
+    glse = torch.zeros_like(lse) if glse is None else glse
+    grads = _bwd_op(gO, glse, h, W, E, bias, O, lse, *ctx.consts, *want)
+    return tuple(x if w else None for x, w in zip(grads, want)) + (None,) * len(ctx.consts)
 
 
-_fwd_op.register_autograd(_autograd_backward, setup_context=_setup_context)
+_fwd_op.register_autograd(_readout_backward, setup_context=_save_readout)
 
 
 def softmax_readout_op(h2, W, E, bias, logit_scale, chunk, cdt):

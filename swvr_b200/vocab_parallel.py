@@ -18,7 +18,7 @@ ranks in tests; the default is libswvr_b200.so and nothing else runs in producti
 """
 from __future__ import annotations
 
-from typing import Optional
+from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -26,7 +26,7 @@ from torch import nn
 
 from . import _native as nat
 from .api import _check, _compute_dtype
-from .ops import (_prepare, _problem, _require_cuda, _workspace, acc_dtype, default_chunk_size, mse_loss_op)
+from .ops import _backward, _forward_state, acc_dtype, default_chunk_size, mse_loss_op
 
 
 def shard_range(V: int, world: int, rank: int):
@@ -35,29 +35,13 @@ def shard_range(V: int, world: int, rank: int):
 
 
 class NativeBackend:
-    """The CUDA library: partial forward, combine and shard backward."""
+    """The CUDA library: partial forward, combine and shard backward.  The engine choice (tensor
+    cores, or the exact SIMT kernels for wide embeddings) and the per-chunk parameter casts of
+    autocast over fp32 parameters are the single-GPU path's (``ops``)."""
 
     @staticmethod
     def partial(h, W, E, bias, scale, chunk, cdt):
-        dev = _require_cuda(h, W, E, bias)
-        adt = acc_dtype(cdt)
-        N, D = h.shape[0], E.shape[1]
-        m2 = torch.empty(N, dtype=adt, device=dev)
-        l = torch.empty(N, dtype=adt, device=dev)
-        acc = torch.empty(N, D, dtype=adt, device=dev)
-        if N == 0:
-            return m2, l, acc
-        if W.shape[0] == 0:
-            return m2.fill_(float("-inf")), l.zero_(), acc.zero_()
-        hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
-        p = _problem(hc, Wc, Ec, b, scale, chunk, cdt)
-        nbytes = nat.c_size_t(0)
-        with torch.cuda.device(dev):
-            nat.check(nat.lib().swvr_fwd_workspace_size(p, nat.ctypes.byref(nbytes)), "swvr_fwd_workspace_size")
-            ws = _workspace(nbytes.value, dev)
-            nat.check(nat.lib().swvr_fwd_partial(p, m2.data_ptr(), l.data_ptr(), acc.data_ptr(), ws.data_ptr(),
-                                                 ws.numel(), nat.stream_ptr(dev)), "swvr_fwd_partial")
-        return m2, l, acc
+        return _forward_state(h, W, E, bias, scale, chunk, cdt)
 
     @staticmethod
     def combine(m2s, ls, accs):
@@ -74,44 +58,10 @@ class NativeBackend:
         return O, lse
 
     @staticmethod
-    def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_W, need_E, need_b):
-        """Returns (dh partial in the accumulation dtype, gW, gE, gb) for this shard."""
-        dev = _require_cuda(h, W, E, bias)
-        adt = O.dtype
-        N, K, V, D = h.shape[0], h.shape[1], W.shape[0], E.shape[1]
-        hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
-        K8 = hc.shape[1]
-        dh = torch.zeros(N, K8, dtype=adt, device=dev)
-        gW = torch.empty(V, K8, dtype=W.dtype if W.dtype in (cdt, torch.float32) else torch.float32,
-                         device=dev) if need_W else None
-        gE = torch.empty(E.shape, dtype=E.dtype, device=dev) if need_E else None
-        gb = torch.empty(bias.shape, dtype=bias.dtype, device=dev) if (need_b and bias is not None) else None
-        if N == 0 or V == 0:
-            for x in (gW, gE, gb):
-                if x is not None:
-                    x.zero_()
-        else:
-            p = _problem(hc, Wc, Ec, b, scale, chunk, cdt)
-            g = nat.Grads()
-            gO = gO.to(adt).contiguous()
-            glse = glse.to(adt).contiguous()
-            g.grad_O, g.grad_lse, g.O, g.lse = gO.data_ptr(), glse.data_ptr(), O.data_ptr(), lse.data_ptr()
-            g.grad_h_acc = dh.data_ptr()
-            if gW is not None:
-                g.grad_W, g.grad_W_dtype, g.ld_grad_W = gW.data_ptr(), nat.dtype_code(gW.dtype), K8
-            if gE is not None:
-                g.grad_E, g.grad_E_dtype, g.ld_grad_E = gE.data_ptr(), nat.dtype_code(gE.dtype), max(D, 1)
-            if gb is not None:
-                g.grad_bias, g.grad_bias_dtype = gb.data_ptr(), nat.dtype_code(gb.dtype)
-            nbytes = nat.c_size_t(0)
-            with torch.cuda.device(dev):
-                nat.check(nat.lib().swvr_bwd_workspace_size(p, g, nat.ctypes.byref(nbytes)), "swvr_bwd_workspace_size")
-                ws = _workspace(nbytes.value, dev)
-                nat.check(nat.lib().swvr_bwd(p, g, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)), "swvr_bwd")
-        dh = dh if K8 == K else dh[:, :K].contiguous()
-        if gW is not None:
-            gW = gW[:, :K].to(W.dtype)
-        return dh, gW, gE, gb
+    def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_h, need_W, need_E, need_b):
+        """(this shard's dh in the accumulation dtype or None, gW, gE, gb)."""
+        return _backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_h, need_W, need_E, need_b,
+                         dh_partial=True)
 
 
 _BACKEND = NativeBackend
@@ -123,13 +73,20 @@ def set_backend(backend) -> None:
     _BACKEND = backend if backend is not None else NativeBackend
 
 
+def _group_name(group) -> str:
+    return (group if group is not None else dist.group.WORLD).group_name
+
+
+def _resolve(group_name: str):
+    return dist.distributed_c10d._resolve_process_group(group_name)
+
+
 def _sum_dh_over_shards(dh: torch.Tensor, out_dtype: torch.dtype, group) -> torch.Tensor:
     """The sum over ranks of the shards' dh partials, in ``out_dtype`` on every rank.
 
     A reduce-scatter in the accumulation dtype (each rank sums one slab of rows, in a fixed
     order) followed by an all-gather of the slabs already cast to h's dtype: the same fp32
-    sum as an all-reduce, with 3/4 of its traffic for a 16-bit h.  Every rank takes both
-    collectives exactly once per backward, frozen h or not."""
+    sum as an all-reduce, with 3/4 of its traffic for a 16-bit h."""
     world = dist.get_world_size(group)
     N, K = dh.shape
     rows = -(-N // world)
@@ -142,34 +99,70 @@ def _sum_dh_over_shards(dh: torch.Tensor, out_dtype: torch.dtype, group) -> torc
     return full[:N]
 
 
-class _VocabParallelReadout(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, h, W, E, bias, scale, chunk, cdt, group):
-        world = dist.get_world_size(group)
-        m2, l, acc = _BACKEND.partial(h, W, E, bias, scale, chunk, cdt)
-        N, D = acc.shape
-        packed = torch.cat([m2[:, None], l[:, None], acc], dim=1).contiguous()
-        gathered = torch.empty(world * N, D + 2, dtype=packed.dtype, device=packed.device)
-        dist.all_gather_into_tensor(gathered, packed, group=group)
-        gathered = gathered.view(world, N, D + 2)
-        O, lse = _BACKEND.combine(gathered[:, :, 0].contiguous(), gathered[:, :, 1].contiguous(),
-                                  gathered[:, :, 2:].contiguous())
-        ctx.save_for_backward(h, W, E, bias, O, lse)
-        ctx.args = (scale, chunk, cdt, group)
-        return O, lse
+# The sharded readout is an opaque custom-op pair like the single-GPU one (ops.py), so
+# torch.compile(fullgraph=True) and activation checkpointing treat it the same way.  The process
+# group travels as its registered name (a custom op's schema has no ProcessGroup type).  The
+# collectives run inside the ops; every rank calls them in the same order, and the ranks must
+# agree on which inputs are frozen (a frozen h skips the dh exchange on every rank).
 
-    @staticmethod
-    def backward(ctx, gO, glse):
-        h, W, E, bias, O, lse = ctx.saved_tensors
-        scale, chunk, cdt, group = ctx.args
-        gO = gO if gO is not None else torch.zeros_like(O)
-        glse = glse if glse is not None else torch.zeros_like(lse)
-        need_h, need_W, need_E, need_b = ctx.needs_input_grad[:4]
-        dh, gW, gE, gb = _BACKEND.backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_W, need_E,
-                                           need_b and bias is not None)
-        gh = _sum_dh_over_shards(dh, h.dtype, group)
-        gh = gh if need_h else None
-        return (gh, gW if need_W else None, gE if need_E else None, gb if need_b else None, None, None, None, None)
+@torch.library.custom_op("swvr_b200::vp_fwd", mutates_args=())
+def _vp_fwd_op(h: torch.Tensor, W: torch.Tensor, E: torch.Tensor, bias: Optional[torch.Tensor], logit_scale: float,
+               chunk: int, cdt: torch.dtype, group_name: str) -> Tuple[torch.Tensor, torch.Tensor]:
+    group = _resolve(group_name)
+    world = dist.get_world_size(group)
+    m2, l, acc = _BACKEND.partial(h, W, E, bias, logit_scale, chunk, cdt)
+    N, D = acc.shape
+    packed = torch.cat([m2[:, None], l[:, None], acc], dim=1).contiguous()
+    gathered = torch.empty(world * N, D + 2, dtype=packed.dtype, device=packed.device)
+    dist.all_gather_into_tensor(gathered, packed, group=group)
+    gathered = gathered.view(world, N, D + 2)
+    return _BACKEND.combine(gathered[:, :, 0].contiguous(), gathered[:, :, 1].contiguous(),
+                            gathered[:, :, 2:].contiguous())
+
+
+@_vp_fwd_op.register_fake
+def _(h, W, E, bias, logit_scale, chunk, cdt, group_name):
+    adt = acc_dtype(cdt)
+    return h.new_empty(h.shape[0], E.shape[1], dtype=adt), h.new_empty(h.shape[0], dtype=adt)
+
+
+@torch.library.custom_op("swvr_b200::vp_bwd", mutates_args=())
+def _vp_bwd_op(gO: torch.Tensor, glse: torch.Tensor, h: torch.Tensor, W: torch.Tensor, E: torch.Tensor,
+               bias: Optional[torch.Tensor], O: torch.Tensor, lse: torch.Tensor, logit_scale: float, chunk: int,
+               cdt: torch.dtype, group_name: str, need_h: bool, need_W: bool, need_E: bool,
+               need_b: bool) -> List[torch.Tensor]:
+    group = _resolve(group_name)
+    dh, gW, gE, gb = _BACKEND.backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W,
+                                       need_E, need_b)
+    gh = _sum_dh_over_shards(dh, h.dtype, group) if need_h else None
+    return [x if x is not None else h.new_empty(0) for x in (gh, gW, gE, gb)]
+
+
+@_vp_bwd_op.register_fake
+def _(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, group_name, need_h, need_W, need_E, need_b):
+    out = []
+    for wanted, param in ((need_h, h), (need_W, W), (need_E, E), (need_b and bias is not None, bias)):
+        out.append(torch.empty_like(param) if wanted else h.new_empty(0))
+    return out
+
+
+def _vp_save(ctx, inputs, output):
+    h, W, E, bias, logit_scale, chunk, cdt, group_name = inputs
+    ctx.save_for_backward(h, W, E, bias, *output)
+    ctx.consts = (logit_scale, chunk, cdt, group_name)
+
+
+def _vp_backward(ctx, gO, glse):
+    h, W, E, bias, O, lse = ctx.saved_tensors
+    want = [bool(x) for x in ctx.needs_input_grad[:4]]
+    want[3] = want[3] and bias is not None
+    gO = torch.zeros_like(O) if gO is None else gO
+    glse = torch.zeros_like(lse) if glse is None else glse
+    grads = _vp_bwd_op(gO, glse, h, W, E, bias, O, lse, *ctx.consts, *want)
+    return tuple(x if w else None for x, w in zip(grads, want)) + (None,) * len(ctx.consts)
+
+
+_vp_fwd_op.register_autograd(_vp_backward, setup_context=_vp_save)
 
 
 def softmax_readout_vocab_parallel(h, W_shard, E_shard, bias_shard=None, *, logit_scale=1.0, chunk_size=None,
@@ -187,7 +180,7 @@ def softmax_readout_vocab_parallel(h, W_shard, E_shard, bias_shard=None, *, logi
         raise ValueError(f"chunk_size must be positive, got {chunk}")
     cdt = _compute_dtype(h, W_shard)
     with torch.autocast(h.device.type, enabled=False):
-        O, lse = _VocabParallelReadout.apply(h2, W_shard, E_shard, bias_shard, float(logit_scale), chunk, cdt, group)
+        O, lse = _vp_fwd_op(h2, W_shard, E_shard, bias_shard, float(logit_scale), chunk, cdt, _group_name(group))
     return O.view(*lead, E_shard.shape[1]), lse.view(lead)
 
 

@@ -84,6 +84,8 @@ def main():
         ap.error("pass --ref <reference checkout> or set SWVR_REFERENCE")
     sys.path.insert(0, args.ref)
     import swvr  # the reference library
+    if not os.path.abspath(swvr.__file__).startswith(os.path.abspath(args.ref)):
+        raise SystemExit(f"imported {swvr.__file__}, not the reference under {args.ref}")
     torch.manual_seed(0)
 
     # fp64 cases from the reference's CPU test-suite (test_cpu.py)

@@ -41,11 +41,11 @@ class OracleBackend:
         return torch.from_numpy(O), torch.from_numpy(lse)
 
     @staticmethod
-    def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_W, need_E, need_b):
+    def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_h, need_W, need_E, need_b):
         b = None if bias is None else bias.detach().numpy()
         gh, gW, gE, gb = orc.chunked_backward(gO.numpy(), glse.numpy(), h.detach().numpy(), W.detach().numpy(),
                                               E.detach().numpy(), b, O.numpy(), lse.numpy(), scale, chunk, "fp64",
-                                              True, need_W, need_E, need_b)
+                                              need_h, need_W, need_E, need_b)
         t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x))
         return t(gh), t(gW), t(gE), t(gb)
 
@@ -232,3 +232,48 @@ def test_ddp_over_vocab_parallel_grid(tmp_path):
         np.testing.assert_allclose(o["gW"], W.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
         np.testing.assert_allclose(o["gE"], E.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
         np.testing.assert_allclose(o["gb"], b.grad[v0:v1].numpy(), rtol=1e-9, atol=1e-12)
+
+
+# ---------------------------------------------------------------------- torch.compile and checkpointing
+def _compile_ckpt_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from swvr_b200 import vocab_parallel as vp
+    vp.set_backend(OracleBackend)
+    h, W, E, b, gO, glse = _inputs()
+    v0, v1 = vp.shard_range(W.shape[0], world, rank)
+
+    def loss_fn(x, Ws, Es, bs):
+        O, lse = vp.softmax_readout_vocab_parallel(x, Ws, Es, bs, logit_scale=0.5, chunk_size=8)
+        return (O * gO).sum() + (lse * glse).sum()
+
+    def leaves():
+        return [h.clone().requires_grad_(True)] + [x[v0:v1].clone().requires_grad_(True) for x in (W, E, b)]
+
+    out = {"v0": v0, "v1": v1}
+    # activation checkpointing: the sharded forward (and its all-gather) re-runs in the backward
+    xs = leaves()
+    torch.utils.checkpoint.checkpoint(loss_fn, *xs, use_reentrant=False).backward()
+    out.update({f"ckpt_{k}": x.grad.numpy() for k, x in zip("hWEb", xs)})
+    # torch.compile with fullgraph=True: the custom-op pair is opaque, so there is no graph break
+    xs = leaves()
+    torch.compile(loss_fn, fullgraph=True, backend="aot_eager")(*xs).backward()
+    out.update({f"comp_{k}": x.grad.numpy() for k, x in zip("hWEb", xs)})
+    np.savez(os.path.join(out_dir, f"cc{rank}.npz"), **out)
+    dist.destroy_process_group()
+
+
+def test_vocab_parallel_under_checkpoint_and_compile(tmp_path):
+    """The sharded readout under ``torch.utils.checkpoint`` and under
+    ``torch.compile(fullgraph=True)`` gives the unsharded gradients on every rank."""
+    world = 2
+    mp.spawn(_compile_ckpt_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    h, W, E, b, gO, glse = (x.numpy() for x in _inputs())
+    ref = dict(zip("hWEb", orc.readout_grads(h, W, E, b, gO, glse, 0.5)))
+    for r in range(world):
+        o = np.load(tmp_path / f"cc{r}.npz")
+        v0, v1 = int(o["v0"]), int(o["v1"])
+        for mode in ("ckpt", "comp"):
+            np.testing.assert_allclose(o[f"{mode}_h"], ref["h"], rtol=1e-10, atol=1e-13)
+            for k in "WEb":
+                np.testing.assert_allclose(o[f"{mode}_{k}"], ref[k][v0:v1], rtol=1e-10, atol=1e-13)

@@ -93,3 +93,44 @@ def test_two_gpu_vocab_parallel_matches_single_gpu(tmp_path):
         assert rel_err(torch.from_numpy(z["gW"]), Wf.grad[v0:v1]) < 2e-2
         assert rel_err(torch.from_numpy(z["gE"]), Ef.grad[v0:v1]) < 2e-2
         assert rel_err(torch.from_numpy(z["gb"]), bf.grad[v0:v1]) < 2e-2
+
+
+@pytest.mark.parametrize("G", [2, 3, 8])
+def test_sharded_compute_on_one_gpu(G):
+    """The vocabulary-sharded path's GPU work on one device: every shard's partial forward
+    (swvr_fwd_partial) and shard backward (dh partial in fp32, local dW / dE / db), merged as
+    the ranks merge them -- states stacked in rank order through swvr_combine, dh partials
+    summed -- with only the NCCL transport replaced by in-process stacking.  Checked against
+    the single-GPU API on the full vocabulary and against the fp64 oracle.  Runs on one GPU, so
+    it needs no second device; the collectives themselves are covered by the gloo CPU tests
+    and the 2-GPU NCCL test above."""
+    import swvr_b200 as swvr
+    from oracle import swvr_oracle as orc
+    from swvr_b200 import vocab_parallel as vp
+    from tests.helpers import npy, rel_err
+
+    h, W, E, b, t, w = (x.cuda() for x in _inputs())
+    cdt = torch.bfloat16
+    spans = [vp.shard_range(V, G, r) for r in range(G)]
+    states = [vp.NativeBackend.partial(h, W[a:z], E[a:z], b[a:z], 1.0, 4096, cdt) for a, z in spans]
+    O, lse = vp.NativeBackend.combine(*(torch.stack([s[i] for s in states]) for i in range(3)))
+    O_ref, lse_ref = swvr.softmax_readout(h, W, E, b, chunk_size=4096)
+    assert rel_err(O, O_ref) < 2e-2
+    assert float((lse - lse_ref).abs().max()) < 1e-2
+    Oo, lo = orc.softmax_readout_reference(npy(h), npy(W), npy(E), npy(b))
+    assert rel_err(O, Oo) < 2e-2 and float(np.abs(npy(lse) - lo).max()) < 1e-2
+
+    g = torch.Generator().manual_seed(9)
+    gO = (0.02 * torch.randn(N, D, generator=g)).cuda()
+    glse = (0.01 * torch.randn(N, generator=g)).cuda()
+    dh = torch.zeros(N, K, dtype=torch.float32, device="cuda")
+    gW, gE, gb = [], [], []
+    for a, z in spans:
+        d, x, y, c = vp.NativeBackend.backward(gO, glse, h, W[a:z], E[a:z], b[a:z], O, lse, 1.0, 4096, cdt,
+                                               True, True, True, True)
+        assert d.dtype == torch.float32 and d.shape == (N, K)
+        dh += d
+        gW.append(x), gE.append(y), gb.append(c)
+    gr = orc.readout_grads(npy(h), npy(W), npy(E), npy(b), npy(gO), npy(glse))
+    for name, got, ref in zip("hWEb", [dh, torch.cat(gW), torch.cat(gE), torch.cat(gb)], gr):
+        assert rel_err(got, ref) < 2e-2, (name, rel_err(got, ref))

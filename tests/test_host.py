@@ -21,6 +21,15 @@ def test_library_exports_every_declared_symbol():
     assert lib.swvr_abi_version() == 2
 
 
+def test_swvr_import_name_is_this_library():
+    """``import swvr`` (the reference's package name) reaches this implementation."""
+    import swvr as alias
+    for name in ("softmax_readout", "softmax_readout_mse", "SoftmaxReadoutMSE", "softmax_readout_reference"):
+        assert getattr(alias, name) is getattr(swvr, name), name
+    assert sorted(alias.__all__) == sorted(swvr.__all__)
+    assert alias.__version__ == swvr.__version__
+
+
 def _problem(N=256, K=64, V=1000, D=16, dt=nat.BF16, ptr=1 << 20, chunk=8192, ld=None):
     p = nat.Problem()
     p.n_tokens, p.hidden, p.vocab, p.embed_dim = N, K, V, D
