@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -176,6 +177,16 @@ static int validate(const swvr_problem* p) {
 }
 
 // ---------------------------------------------------------------------------- forward plan
+// Token tiles per group of the forward's unit order (tc::fwd_unit); SWVR_FWD_GROUP overrides
+// the default.
+static int fwd_group(int MT) {
+  static const int v = [] {
+    const char* s = std::getenv("SWVR_FWD_GROUP");
+    return s ? std::max(1, std::atoi(s)) : 1;
+  }();
+  return std::max(1, std::min(v, std::max(MT, 1)));
+}
+
 struct FwdPlan {
   int DP, MT, VT, splits, per, units, pairs;
   size_t off_m2, off_l, off_acc, bytes;
@@ -236,6 +247,7 @@ static int tc_fwd_launch(const swvr_problem& p, const FwdPlan& f, char* scratch,
   prm.splits = f.splits;
   prm.per = f.per;
   prm.units = f.units;
+  prm.gm = fwd_group(f.MT);
   prm.part_m2 = reinterpret_cast<float*>(scratch + f.off_m2);
   prm.part_l = reinterpret_cast<float*>(scratch + f.off_l);
   prm.part_acc = reinterpret_cast<float*>(scratch + f.off_acc);
@@ -262,6 +274,16 @@ static int tc_fwd(const swvr_problem& p, void* O, void* lse, void* m2o, void* lo
 }
 
 // ---------------------------------------------------------------------------- backward plan
+// gO and E of the score kernel come from their own producer warp (1, the default) or are
+// interleaved with the W / h stream (0); SWVR_BWD_AUX_LOADS overrides the default.
+static int bwd_aux_loads() {
+  static const int v = [] {
+    const char* s = std::getenv("SWVR_BWD_AUX_LOADS");
+    return s ? (std::atoi(s) != 0 ? 1 : 0) : 1;
+  }();
+  return v;
+}
+
 static void choose_ts(int VTc, int NT, int sms, int* TS, int* per_t) {
   int best = 1;
   int64_t best_cost = -1;
@@ -418,6 +440,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     sp.ld_ds = b.Npad;
     sp.part_de = part_de;
     sp.part_db = part_db;
+    sp.aux_loads = bwd_aux_loads();
     if (b.need_ds) {
       SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
       SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));

@@ -16,12 +16,26 @@ struct FwdParams {
   int bias_dt;
   int MT, VT;             // 256-token pair tiles, vocabulary tiles
   int splits, per, units; // vocabulary splits per token tile, tiles per split, MT * splits
+  int gm;                 // unit order: groups of gm token tiles walk the splits split-major
   float* part_m2;         // [units * 256]
   float* part_l;          // [units * 256]
   float* part_acc;        // [units * 256 * D]
 };
 
 constexpr int kFwdTokenTile = 256;  // tokens per work unit (a CTA pair, 128 per CTA)
+
+// Work unit u -> (token tile mt, vocabulary split sp).  Consecutive units run at the same time
+// on consecutive pairs, so the order decides which W slices are streamed together: groups of
+// gm token tiles take the splits one after another (gm = 1: every split of a token tile in a
+// row; gm >= MT: one split for all token tiles).  The partial-state slot of a unit is
+// mt * splits + sp whatever the order.
+__host__ __device__ inline void fwd_unit(const FwdParams& p, int u, int* mt, int* sp) {
+  const int gsize = p.gm * p.splits;
+  const int grp = u / gsize, r = u % gsize;
+  const int rows = min(p.gm, p.MT - grp * p.gm);  // token tiles in this (possibly last, short) group
+  *sp = r / rows;
+  *mt = grp * p.gm + r % rows;
+}
 
 int fwd_vocab_tile(int DP);  // vocabulary rows per tile: 192 (DP <= 128) or 128 (DP 256)
 int fwd_o_width(int DP);     // the O MMA's N: 128 or 256; each CTA stages half of it
@@ -51,6 +65,7 @@ struct BwdScoresParams {
   int64_t ld_ds;
   float* part_de;      // [units * 256 * D] or null
   float* part_db;      // [units * 256] or null
+  int aux_loads;       // 1: warp 2 loads gO and E, so the W / h stream never waits on their buffers
 };
 
 struct BwdScoresMaps {

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(256, 1)
               stage = 0;
               sphase ^= 1u;
             }
-            if (kb == kx) {
+            if (kb == kx && !p.aux_loads) {
               {
                 // gO, K-major: this CTA's DPC/2 tokens of each dP chunk
                 const uint32_t kbuf = g % Cfg::GOK_NB;
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(256, 1)
                                    static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, gom_tile * BN);
               }
             }
-            if (it == it0 && kb == (Cfg::kSingleS ? kx : KB - 1)) {
+            if (!p.aux_loads && it == it0 && kb == (Cfg::kSingleS ? kx : KB - 1)) {
               // E of this unit.  With double-buffered S the previous unit's last dP chunks
               // may still be issued during this tile's S loop, so E is replaced at its end.
               if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
@@ -250,8 +250,70 @@ __global__ void __launch_bounds__(256, 1)
         }
         ++uc;
       }
-      if (!Cfg::kSingleS && g > 0) {
+      if (!p.aux_loads && !Cfg::kSingleS && g > 0) {
         // the pair's last tile: its MN-major gO, once the previous tile's dE has read the buffer
+        if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+        if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+        const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+        for (int c = 0; c < Cfg::GOM_NB; ++c)
+          tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                           static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, prev_it * BN);
+      }
+    }
+  } else if (warp == 2) {
+    if (lane == 0 && p.aux_loads) {
+      // ------------------------------------------------ gO / E producer (both CTAs, aux_loads)
+      // The same loads, waits and buffers as the interleaved path above, in the order the MMA
+      // thread consumes them: per tile, the unit's E (first tile), the tile's K-major gO, and
+      // the MN-major gO of the tile whose dE comes next.  The W / h stream of warp 0 then
+      // never waits on these buffers.
+      uint32_t g = 0, uc = 0;
+      int prev_it = 0;
+      for (int u = pair; u < p.units; u += npairs) {
+        const int vt = u / p.TS, ts = u % p.TS;
+        const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
+        if (it1 <= it0) continue;
+        const int vrow0 = p.v_begin + vt * 256 + static_cast<int>(rank) * 128;
+        for (int it = it0; it < it1; ++it, ++g) {
+          if (it == it0) {
+            if (!mbar_wait(e_empty, (uc & 1u) ^ 1u, abort_flag, kErrBwdScores | 1)) goto done;
+            if (leader) mbar_arrive_expect_tx(e_full, 2 * Cfg::E_BYTES);
+            const uint32_t eb = mapa_shared(smem_u32(e_full), 0);
+#pragma unroll
+            for (int c = 0; c < DP / 64; ++c)
+              tma_load_2d_pair(smem + Cfg::SMEM_E + c * Cfg::BOX, &tm_e, eb, c * 64, vrow0);
+          }
+          {
+            const uint32_t kbuf = g % Cfg::GOK_NB;
+            if (!mbar_wait(&gok_empty[kbuf], ((g / Cfg::GOK_NB) & 1u) ^ 1u, abort_flag, kErrBwdScores | 3))
+              goto done;
+            if (leader) mbar_arrive_expect_tx(&gok_full[kbuf], 2 * Cfg::GOK_BYTES);
+            const uint32_t gb = mapa_shared(smem_u32(&gok_full[kbuf]), 0);
+#pragma unroll
+            for (int jj = 0; jj < Cfg::NCH; ++jj)
+#pragma unroll
+              for (int c = 0; c < DP / 64; ++c)
+                tma_load_2d_pair(smem + Cfg::SMEM_GOK + kbuf * Cfg::GOK_BYTES + jj * Cfg::GOK_CH + c * Cfg::GOK_CBOX,
+                                 &tm_gok, gb, c * 64,
+                                 it * BN + jj * Cfg::DPC + static_cast<int>(rank) * (Cfg::DPC / 2));
+          }
+          if (Cfg::kSingleS || g > 0) {
+            const uint32_t fill = Cfg::kSingleS ? g : g - 1u;
+            const int gom_tile = Cfg::kSingleS ? it : prev_it;
+            if (!mbar_wait(gom_empty, (fill & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
+            if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
+            const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);
+#pragma unroll
+            for (int c = 0; c < Cfg::GOM_NB; ++c)
+              tma_load_2d_pair(smem + Cfg::SMEM_GOM + c * Cfg::GOM_BOX, &tm_gom, mb,
+                               static_cast<int>(rank) * Cfg::GOM_W + c * Cfg::GOM_BW, gom_tile * BN);
+          }
+          prev_it = it;
+        }
+        ++uc;
+      }
+      if (!Cfg::kSingleS && g > 0) {
         if (!mbar_wait(gom_empty, ((g - 1u) & 1u) ^ 1u, abort_flag, kErrBwdScores | 4)) goto done;
         if (leader) mbar_arrive_expect_tx(gom_full, 2 * Cfg::GOM_BYTES);
         const uint32_t mb = mapa_shared(smem_u32(gom_full), 0);

@@ -16,9 +16,10 @@
 // which bounds the single-CTA kernel, drops below the MMA rate.  Warp roles: warp 0 issues
 // TMA loads, warp 1 (one thread, even CTA) issues MMAs, warps 4-7 run the online softmax.
 // S is double-buffered in TMEM (2 x BV columns, O in the last 128 or 256), so the MMAs of tile
-// j+1 overlap the softmax of tile j.  The running reference max m_ref is only raised when
-// a chunk's max exceeds it by more than 2^kEmergency (exact either way because l and O
-// share m_ref); then O is rescaled in TMEM.
+// j+1 overlap the softmax of tile j.  The running reference m_ref (a whole number, in log2
+// units) is only raised when a chunk's max exceeds it by more than kEmergency octaves (exact
+// either way because l and O share m_ref); it then rises by a whole number of octaves, so P
+// already in TMEM, l and O are rescaled by an exact power of two.
 //
 // Each unit writes its per-row state (m_ref in log2 units, l, O-accumulator) to a partial
 // slot; combine_kernel (small.cu) merges the slots of a row in a fixed order.
@@ -127,7 +128,8 @@ __global__ void __launch_bounds__(256, 1)
       // ------------------------------------------------------------ TMA producer (both CTAs)
       uint32_t stage = 0, sphase = 0, g = 0;
       for (int u = pair; u < p.units; u += npairs) {
-        const int mt = u / p.splits, sp = u % p.splits;
+        int mt, sp;
+        fwd_unit(p, u, &mt, &sp);
         const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
         const int hrow = mt * 256 + static_cast<int>(rank) * 128;
         for (int vt = vt0; vt < vt1; ++vt, ++g) {
@@ -168,7 +170,8 @@ __global__ void __launch_bounds__(256, 1)
       const uint64_t db0 = sdesc_sw128(smem_u32(smem + Cfg::SMEM_B), 16, 1024);
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
       for (int u = pair; u < p.units; u += npairs) {
-        const int sp = u % p.splits;
+        int mt, sp;
+        fwd_unit(p, u, &mt, &sp);
         const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
         const int ntiles = vt1 - vt0;
         if (ntiles <= 0) continue;
@@ -216,9 +219,10 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // -------------------------------------------------------------- softmax warps (both CTAs)
     // One pass per tile.  P = 2^(t - ref) with t = S*s*log2e + b*log2e and ref the running
-    // reference max.  A 32-column chunk whose max exceeds ref + kEmergency raises ref to
-    // that max and rescales the P chunks of this tile already in TMEM, l, and (after the
-    // previous P.E completed) O.
+    // reference, a whole number.  A 32-column chunk whose max cm exceeds ref + kEmergency
+    // raises ref to ref + ceil(cm - ref) (ceil(cm) from -inf) and rescales the P chunks of this
+    // tile already in TMEM, l, and (after the previous P.E completed) O by 2^(old - new), an
+    // exact power of two: the rescaled 16-bit P values keep their single rounding.
     const int r = threadIdx.x - 128;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t trow = tmem + lane_base;
@@ -227,7 +231,8 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t o_free_leader = mapa_shared(smem_u32(o_free), 0);
     uint32_t g = 0;
     for (int u = pair; u < p.units; u += npairs) {
-      const int mt = u / p.splits, sp = u % p.splits;
+      int mt, sp;
+        fwd_unit(p, u, &mt, &sp);
       const int vt0 = sp * p.per, vt1 = min(vt0 + p.per, p.VT);
       if (vt1 <= vt0) continue;
       const int n = mt * 256 + static_cast<int>(rank) * 128 + r;
@@ -272,11 +277,21 @@ __global__ void __launch_bounds__(256, 1)
           for (int i = 1; i < 32; ++i) cm = fmaxf(cm, t[i]);
           const bool emerg = cm > ref + Cfg::kEmergency;
           if (__any_sync(0xffffffffu, emerg)) {
-            const float newref = emerg ? cm : ref;
-            const float alpha = newref == ref ? 1.f : ex2(ref - newref);
+            // ref stays a whole number: it rises by whole octaves, so the rescale factor is an
+            // exact power of two and rescaled 16-bit P values are exact (no second rounding)
+            float newref = ref, alpha = 1.f;
+            if (emerg) {
+              if (ref == -INFINITY) {
+                newref = ceilf(cm);
+                alpha = 0.f;  // nothing finite was written before
+              } else {
+                const float k = ceilf(cm - ref);
+                newref = ref + k;
+                alpha = exp2_neg_int(k);
+              }
+            }
             if (c > 0) {
-              // rescale this tile's P chunks already written (16-bit pairs): their products are
-              // rounded to 16 bits again, so those P values carry a second rounding
+              // rescale this tile's P chunks already written (16-bit pairs) by the power of two
 #pragma unroll 1
               for (int cc = 0; cc < c; ++cc) {
                 uint32_t pk[16];
@@ -309,7 +324,7 @@ __global__ void __launch_bounds__(256, 1)
           if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 8)) goto done;
           tc_fence_after();
           if (__any_sync(0xffffffffu, ref != ref_start)) {
-            const float alpha = ref == ref_start ? 1.f : ex2(ref_start - ref);
+            const float alpha = ref == ref_start ? 1.f : (ref_start == -INFINITY ? 0.f : exp2_neg_int(ref - ref_start));
 #pragma unroll 1
             for (int c = 0; c < p.D; c += 32) {
               uint32_t o[32];
@@ -330,7 +345,7 @@ __global__ void __launch_bounds__(256, 1)
       if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 9)) goto done;
       tc_fence_after();
       {
-        const int64_t slot = static_cast<int64_t>(u) * 256 + static_cast<int>(rank) * 128 + r;
+        const int64_t slot = static_cast<int64_t>(mt * p.splits + sp) * 256 + static_cast<int>(rank) * 128 + r;
 #pragma unroll 1
         for (int c = 0; c < p.D; c += 32) {
           uint32_t o[32];

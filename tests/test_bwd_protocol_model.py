@@ -1,8 +1,9 @@
 """A model of the backward score kernel's barrier protocol (swvr_b200/csrc/tc_bwd.cu).
 
 bwd_scores_kernel is four roles that hand buffers to each other through mbarriers: the TMA
-producer of each CTA, the MMA-issuing thread of the pair, the tensor pipe (which executes
-issued MMAs and commits in order) and the gradient warps of each CTA.  This model restates
+producer of each CTA (with ``aux_loads`` a second one, warp 2, loads gO and E), the
+MMA-issuing thread of the pair, the tensor pipe (which executes issued MMAs and commits in
+order) and the gradient warps of each CTA.  This model restates
 each role's loop, waits and arrivals as Python generators (same counters, same parity
 expressions, same order as the kernel), runs them under randomised interleavings, and
 checks:
@@ -26,6 +27,7 @@ from tests.protocol_model import Bar, Wait, schedule
 
 def run(cfg, seed, skip_dp_free_test=False):
     NS, KB, NCH, single, need_de, units = cfg["NS"], cfg["KB"], cfg["NCH"], cfg["single"], cfg["need_de"], cfg["units"]
+    aux = cfg.get("aux", False)
     GOK_NB = 2 if NCH > 1 else 1
     kx = min(NS, KB - 1)
     # barriers: leader-only (issuer waits) and per-CTA copies (multicast commits)
@@ -90,7 +92,7 @@ def run(cfg, seed, skip_dp_free_test=False):
                     stage += 1
                     if stage == NS:
                         stage, sphase = 0, sphase ^ 1
-                    if kb == kx:
+                    if kb == kx and not aux:
                         kbuf = g % GOK_NB
                         f = g // GOK_NB
                         yield Wait(gok_empty[rank][kbuf], (f & 1) ^ 1, f - 1)
@@ -105,7 +107,7 @@ def run(cfg, seed, skip_dp_free_test=False):
                                 assert (fill - 1) in st["de_exec"], ("gom overwrite", fill)
                             gom_full.arrive(fill)
                             st["gom_loaded"][rank].add(fill)
-                    if it == it0 and kb == (kx if single else KB - 1):
+                    if not aux and it == it0 and kb == (kx if single else KB - 1):
                         yield Wait(e_empty[rank], (uc & 1) ^ 1, uc - 1)
                         prevs = [u for u in range(ui) if units[u][1] > units[u][0]]
                         if prevs:
@@ -116,13 +118,56 @@ def run(cfg, seed, skip_dp_free_test=False):
                 prev_it = it
                 g += 1
             uc += 1
-        if not single and g > 0:
+        if not aux and not single and g > 0:
             fill = g - 1
             yield Wait(gom_empty[rank], (fill & 1) ^ 1, fill - 1)
             if need_de and fill - 1 >= 0:
                 assert (fill - 1) in st["de_exec"], "gom overwrite (tail)"
             gom_full.arrive(fill)
             st["gom_loaded"][rank].add(fill)
+
+    def load_e(rank, ui, uc):
+        yield Wait(e_empty[rank], (uc & 1) ^ 1, uc - 1)
+        prevs = [u for u in range(ui) if units[u][1] > units[u][0]]
+        if prevs:
+            prev_tiles = [t for t in range(T) if tiles[t][0] == prevs[-1]]
+            assert all(st["dp_of_tile_exec"].get(t, 0) == NCH for t in prev_tiles), "E overwrite"
+        e_full.arrive(uc)
+        st["e_loaded"][rank].add(ui)
+
+    def load_gok(rank, g):
+        kbuf = g % GOK_NB
+        f = g // GOK_NB
+        yield Wait(gok_empty[rank][kbuf], (f & 1) ^ 1, f - 1)
+        if g - GOK_NB >= 0:
+            assert st["dp_of_tile_exec"].get(g - GOK_NB, 0) == NCH, ("gok overwrite", g)
+        gok_full[kbuf].arrive(f)
+        st["gok_loaded"][rank].add(g)
+
+    def load_gom(rank, fill):
+        yield Wait(gom_empty[rank], (fill & 1) ^ 1, fill - 1)
+        if need_de and fill - 1 >= 0:
+            assert (fill - 1) in st["de_exec"], ("gom overwrite", fill)
+        gom_full.arrive(fill)
+        st["gom_loaded"][rank].add(fill)
+
+    def aux_producer(rank):
+        """warp 2 (aux_loads): per tile the unit's E (first tile), the K-major gO, and the
+        MN-major gO of the tile whose dE comes next, each once its buffer is free."""
+        g = uc = 0
+        for ui, (it0, it1) in enumerate(units):
+            if it1 <= it0:
+                continue
+            for it in range(it0, it1):
+                if it == it0:
+                    yield from load_e(rank, ui, uc)
+                yield from load_gok(rank, g)
+                if single or g > 0:
+                    yield from load_gom(rank, g if single else g - 1)
+                g += 1
+            uc += 1
+        if not single and g > 0:
+            yield from load_gom(rank, g - 1)
 
     def issue(op):
         st["pipe"].append(op)
@@ -310,6 +355,8 @@ def run(cfg, seed, skip_dp_free_test=False):
             uc += 1
 
     roles = {"p0": producer(0), "p1": producer(1), "mma": issuer(), "g0": grad(0), "g1": grad(1)}
+    if aux:
+        roles.update(a0=aux_producer(0), a1=aux_producer(1))
     schedule(roles, st["pipe"], pipe_step, seed)
 
 
@@ -326,7 +373,7 @@ def _configs(n, seed=1):
         if all(b <= a for a, b in units):
             units.append((t, t + 1))
         out.append(dict(NS=rnd.choice([2, 3, 4]), KB=rnd.choice([1, 2, 3, 4, 7, 20]), NCH=nch, single=single,
-                        need_de=rnd.random() < 0.8, units=units))
+                        need_de=rnd.random() < 0.8, units=units, aux=rnd.random() < 0.6))
     return out
 
 
@@ -340,12 +387,13 @@ def test_protocol_holds_under_random_interleavings(idx):
         run(cfg, seed=idx * 10 + s)
 
 
-def test_a_missing_wait_is_caught():
+@pytest.mark.parametrize("aux", [False, True])
+def test_a_missing_wait_is_caught(aux):
     """A planted mistake: the MMA thread issues a tile's later dP chunks between S stages
     without testing that both CTAs' gradient passes have read the previous chunk.  The model
     must flag it (the dP buffer overwritten while read, or a barrier arrival in the wrong
     phase) in some interleaving."""
-    cfg = dict(NS=3, KB=6, NCH=3, single=False, need_de=True, units=[(0, 4), (4, 8)])
+    cfg = dict(NS=3, KB=6, NCH=3, single=False, need_de=True, units=[(0, 4), (4, 8)], aux=aux)
     caught = 0
     for s in range(40):
         try:

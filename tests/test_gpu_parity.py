@@ -537,3 +537,28 @@ def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
     a, b = res["128"], res["192"]
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
     assert rel_err(b[2], a[2]) < 1e-3 and rel_err(b[3], a[3]) < 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_reference_rise_inside_a_tile(dtype):
+    """Scores that climb past the forward's emergency margin (64 octaves for bf16, 8 for fp16)
+    inside a 192-column tile while the values just under the margin stay significant: the
+    running reference rises by whole octaves and the 16-bit P values already in tensor memory
+    are rescaled by an exact power of two.  Checked against the fp64 oracle."""
+    m = 64.0 if dtype == torch.bfloat16 else 8.0
+    N, K, V, D = 130, 64, 1000, 16
+    g = torch.Generator().manual_seed(21)
+    # log2-unit pattern of each 192-column tile, per 32-column block: ~0 (sets the reference),
+    # just under the margin, just over it (first rise), under the next margin, over it, near it
+    base = torch.tensor([-0.3, m - 0.3, m + 0.4, 2 * m + 0.2, 2 * m + 1.5, 2 * m + 1.8], dtype=f64)
+    col = torch.arange(V)
+    t = base[(col % 192) // 32] + 0.1 * torch.rand(V, generator=g, dtype=f64)
+    b = (t * np.log(2.0)).to(torch.float32)                        # fp32 bias: no 16-bit rounding of t
+    h = torch.randn(N, K, generator=g).to(dtype)
+    W = (0.05 * K ** -0.5 * torch.randn(V, K, generator=g)).to(dtype)  # rows differ by a few hundredths
+    E = torch.randn(V, D, generator=g).to(dtype)
+    O, lse = swvr.softmax_readout(h.cuda(), W.cuda(), E.cuda(), b.cuda())
+    Or, lr = orc.softmax_readout_reference(npy(h), npy(W), npy(E), npy(b))
+    assert torch.isfinite(O).all() and torch.isfinite(lse).all()
+    assert rel_err(O, Or) < 2e-2, rel_err(O, Or)
+    assert np.abs(npy(lse) - lr).max() < 1e-2
