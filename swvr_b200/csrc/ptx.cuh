@@ -364,12 +364,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^-k for a whole number k >= 0 held in a float, built from the exponent bits: exact, and 0
-// once 2^-k would fall below the smallest normal float.
-__device__ __forceinline__ float exp2_neg_int(float k) {
-  return k >= 127.f ? 0.f : __int_as_float((127 - static_cast<int>(k)) << 23);
-}
-
 // Packed fp32 pair arithmetic (sm_100 f32x2 instructions).
 __device__ __forceinline__ uint64_t f2_bits(float2 v) {
   uint64_t r;

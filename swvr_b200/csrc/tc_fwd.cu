@@ -16,10 +16,10 @@
 // which bounds the single-CTA kernel, drops below the MMA rate.  Warp roles: warp 0 issues
 // TMA loads, warp 1 (one thread, even CTA) issues MMAs, warps 4-7 run the online softmax.
 // S is double-buffered in TMEM (2 x BV columns, O in the last 128 or 256), so the MMAs of tile
-// j+1 overlap the softmax of tile j.  The running reference m_ref (a whole number, in log2
-// units) is only raised when a chunk's max exceeds it by more than kEmergency octaves (exact
-// either way because l and O share m_ref); it then rises by a whole number of octaves, so P
-// already in TMEM, l and O are rescaled by an exact power of two.
+// j+1 overlap the softmax of tile j.  The running reference m_ref (log2 units) is only raised
+// when a tile's max exceeds it by more than kEmergency octaves (exact either way because l and
+// O share m_ref), and then to that max before any P of the tile is written: only l and O (fp32)
+// are rescaled, so every 16-bit P value carries one rounding.
 //
 // Each unit writes its per-row state (m_ref in log2 units, l, O-accumulator) to a partial
 // slot; combine_kernel (small.cu) merges the slots of a row in a fixed order.
@@ -219,10 +219,10 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // -------------------------------------------------------------- softmax warps (both CTAs)
     // One pass per tile.  P = 2^(t - ref) with t = S*s*log2e + b*log2e and ref the running
-    // reference, a whole number.  A 32-column chunk whose max cm exceeds ref + kEmergency
-    // raises ref to ref + ceil(cm - ref) (ceil(cm) from -inf) and rescales the P chunks of this
-    // tile already in TMEM, l, and (after the previous P.E completed) O by 2^(old - new), an
-    // exact power of two: the rescaled 16-bit P values keep their single rounding.
+    // reference.  Two passes over the tile's S in TMEM: the first finds the tile's max tm of t;
+    // if tm exceeds ref + kEmergency, ref becomes tm and l and (after the previous P.E
+    // completed) O are rescaled by 2^(old - new) in fp32; the second writes P.  P values are
+    // bounded by 2^kEmergency, finite in 16 bits, and never rescaled.
     const int r = threadIdx.x - 128;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t trow = tmem + lane_base;
@@ -251,14 +251,14 @@ __global__ void __launch_bounds__(256, 1)
         if (!warp_wait(&s_full[b], (g >> 1) & 1u, abort_flag, kErrFwd | 7)) goto done;
         tc_fence_after();
         const uint32_t sbase = trow + b * BV;
-        const float ref_start = ref;
-        float2 lsum = make_float2(0.f, 0.f);
+        // pass 1: the tile's max of t.  The reference moves at most once per tile, before any P
+        // of the tile is written, so no P value is ever rescaled (each keeps one 16-bit rounding)
+        float tm = -INFINITY;
 #pragma unroll 1
         for (int c = 0; c < BV / 32; ++c) {
           uint32_t x[32];
           tmem_ld32(sbase + c * 32, x);
           tmem_wait_ld();
-          float t[32];
           const float4* b4 = reinterpret_cast<const float4*>(bt + c * 32);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -267,54 +267,39 @@ __global__ void __launch_bounds__(256, 1)
                                     make_float2(p.sc2, p.sc2), make_float2(bb.x, bb.y));
             const float2 t1 = ffma2(make_float2(__uint_as_float(x[4 * q + 2]), __uint_as_float(x[4 * q + 3])),
                                     make_float2(p.sc2, p.sc2), make_float2(bb.z, bb.w));
-            t[4 * q] = t0.x;
-            t[4 * q + 1] = t0.y;
-            t[4 * q + 2] = t1.x;
-            t[4 * q + 3] = t1.y;
+            tm = fmaxf(tm, fmaxf(fmaxf(t0.x, t0.y), fmaxf(t1.x, t1.y)));
           }
-          float cm = t[0];
-#pragma unroll
-          for (int i = 1; i < 32; ++i) cm = fmaxf(cm, t[i]);
-          const bool emerg = cm > ref + Cfg::kEmergency;
-          if (__any_sync(0xffffffffu, emerg)) {
-            // ref stays a whole number: it rises by whole octaves, so the rescale factor is an
-            // exact power of two and rescaled 16-bit P values are exact (no second rounding)
-            float newref = ref, alpha = 1.f;
-            if (emerg) {
-              if (ref == -INFINITY) {
-                newref = ceilf(cm);
-                alpha = 0.f;  // nothing finite was written before
-              } else {
-                const float k = ceilf(cm - ref);
-                newref = ref + k;
-                alpha = exp2_neg_int(k);
-              }
-            }
-            if (c > 0) {
-              // rescale this tile's P chunks already written (16-bit pairs) by the power of two
+        }
+        // a tile whose max exceeds ref + kEmergency sets ref to that max: l now, O below
+        const float ref_start = ref;
+        float alpha = 1.f;
+        if (tm > ref + Cfg::kEmergency) {
+          alpha = ref == -INFINITY ? 0.f : ex2(ref - tm);
+          ref = tm;
+          l *= alpha;
+        }
+        const float refe = ref == -INFINITY ? 0.f : ref;
+        // pass 2: P = 2^(t - ref), summed unrounded into l and stored rounded over S
+        float2 lsum = make_float2(0.f, 0.f);
 #pragma unroll 1
-              for (int cc = 0; cc < c; ++cc) {
-                uint32_t pk[16];
-                tmem_ld16(sbase + cc * 16, pk);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) pk[i] = scale2<kBF16>(pk[i], alpha);
-                tmem_st16(sbase + cc * 16, pk);
-              }
-              tmem_wait_st();
-            }
-            l *= alpha;
-            lsum.x *= alpha;
-            lsum.y *= alpha;
-            ref = newref;
-          }
-          const float refe = ref == -INFINITY ? 0.f : ref;
+        for (int c = 0; c < BV / 32; ++c) {
+          uint32_t x[32];
+          tmem_ld32(sbase + c * 32, x);
+          tmem_wait_ld();
+          const float4* b4 = reinterpret_cast<const float4*>(bt + c * 32);
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = ex2(t[i] - refe), p1 = ex2(t[i + 1] - refe);
-            lsum = fadd2(lsum, make_float2(p0, p1));
-            pk[i / 2] = pack2<kBF16>(p0, p1);
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = b4[q];
+            const float2 t0 = ffma2(make_float2(__uint_as_float(x[4 * q]), __uint_as_float(x[4 * q + 1])),
+                                    make_float2(p.sc2, p.sc2), make_float2(bb.x, bb.y));
+            const float2 t1 = ffma2(make_float2(__uint_as_float(x[4 * q + 2]), __uint_as_float(x[4 * q + 3])),
+                                    make_float2(p.sc2, p.sc2), make_float2(bb.z, bb.w));
+            const float2 p0 = make_float2(ex2(t0.x - refe), ex2(t0.y - refe));
+            const float2 p1 = make_float2(ex2(t1.x - refe), ex2(t1.y - refe));
+            lsum = fadd2(lsum, fadd2(p0, p1));
+            pk[2 * q] = pack2<kBF16>(p0.x, p0.y);
+            pk[2 * q + 1] = pack2<kBF16>(p1.x, p1.y);
           }
           tmem_st16(sbase + c * 16, pk);
         }
@@ -324,7 +309,6 @@ __global__ void __launch_bounds__(256, 1)
           if (!warp_wait(pe_done, (g - 1u) & 1u, abort_flag, kErrFwd | 8)) goto done;
           tc_fence_after();
           if (__any_sync(0xffffffffu, ref != ref_start)) {
-            const float alpha = ref == ref_start ? 1.f : (ref_start == -INFINITY ? 0.f : exp2_neg_int(ref - ref_start));
 #pragma unroll 1
             for (int c = 0; c < p.D; c += 32) {
               uint32_t o[32];

@@ -2,16 +2,15 @@
 softmax warps), checked against the exact softmax on adversarial logits (CPU only).
 
 The kernel works in base-2 units, t = S*s*log2(e) + b*log2(e).  Per 192-column vocabulary
-tile it reads 32-column blocks; the running reference ``ref`` is a whole number.  A block
-whose max cm exceeds ``ref`` by more than kEmergency octaves (64 for bf16, 8 for fp16) raises
-``ref`` by ceil(cm - ref) octaves (to ceil(cm) from -inf), and the tile's P values already
-written (16-bit), l and the running sum are multiplied by 2^(old - new), an exact power of two,
-so the rescaled P values keep a single 16-bit rounding.  P = 2^(t - ref) is summed unrounded
-into l (fp32) and rounded to 16 bits for O += P.E (fp32 accumulation); once per tile O is
-rescaled by the same kind of factor if ``ref`` moved.  O = acc / l and
+tile it makes two passes over S: the first finds the tile's max tm; if tm exceeds the running
+reference ``ref`` by more than kEmergency octaves (64 for bf16, 8 for fp16), ``ref`` becomes
+tm and l (now) and O (after the previous P.E) are multiplied by 2^(old - new) in fp32; the
+second pass writes P = 2^(t - ref), summed unrounded into l (fp32) and rounded to 16 bits for
+O += P.E (fp32 accumulation).  No P value is rescaled after it was rounded.  O = acc / l and
 LSE = (ref + log2 l) ln 2.  The model restates those steps in numpy with the same roundings
 and checks finiteness and the 16-bit error bound where the reference's own algorithm would
-also be finite, and that every P value of a tile carries one rounding after its rescales.
+also be finite, that every P value carries one rounding, and that a dominant token gives
+O == E exactly.
 """
 import numpy as np
 import pytest
@@ -21,14 +20,9 @@ from oracle import swvr_oracle as orc
 LN2 = np.log(2.0)
 
 
-def _exp2_neg_int(k):
-    """2^-k for a whole number k >= 0 (0 below the smallest normal float), as the kernel builds it."""
-    return np.float32(0.0) if k >= 127 else np.float32(2.0 ** -int(k))
-
-
 def kernel_row(t, E, cdt="bf16", tile=192, block=32, trace=None):
     """O [D] and LSE of one row as fwd_kernel computes them (float32 state, 16-bit P).  With a
-    list ``trace``, each tile's final (t, P, ref) is appended to it."""
+    list ``trace``, each tile's (t, P, ref) is appended to it."""
     f32 = np.float32
     k_emergency = f32(64.0 if cdt == "bf16" else 8.0)
     rnd = (lambda x: orc.round_bf16(x)) if cdt == "bf16" else (lambda x: orc.round_fp16(x))
@@ -37,27 +31,19 @@ def kernel_row(t, E, cdt="bf16", tile=192, block=32, trace=None):
     acc = np.zeros(E.shape[1], dtype=f32)
     for v0 in range(0, len(t), tile):
         tt = t[v0:v0 + tile].astype(f32)
-        ref_start = ref
-        P = np.zeros(len(tt), dtype=f32)
+        ref_start, alpha = ref, f32(1.0)
+        tm = tt.max()                                  # pass 1
+        if tm > ref + k_emergency:
+            alpha = f32(0.0) if ref == -np.inf else f32(np.exp2(f32(ref - tm)))
+            ref, l = tm, f32(l * alpha)
+        refe = f32(0.0) if ref == -np.inf else ref
+        p = np.exp2(tt - refe).astype(f32)             # pass 2
         lsum = f32(0.0)
-        for c0 in range(0, len(tt), block):
-            x = tt[c0:c0 + block]
-            cm = x.max()
-            if cm > ref + k_emergency:
-                if ref == -np.inf:
-                    newref, alpha = f32(np.ceil(cm)), f32(0.0)
-                else:
-                    k = f32(np.ceil(f32(cm - ref)))
-                    newref, alpha = f32(ref + k), _exp2_neg_int(k)
-                P[:c0] = (P[:c0] * alpha).astype(f32)  # a power of two: no second rounding
-                l, lsum, ref = f32(l * alpha), f32(lsum * alpha), newref
-            refe = f32(0.0) if ref == -np.inf else ref
-            p = np.exp2(x - refe).astype(f32)
-            lsum = f32(lsum + p.sum(dtype=f32))
-            P[c0:c0 + block] = rnd(p.astype(np.float64)).astype(f32)
+        for c0 in range(0, len(tt), block):            # the kernel sums block by block
+            lsum = f32(lsum + p[c0:c0 + block].sum(dtype=f32))
+        P = rnd(p.astype(np.float64)).astype(f32)
         l = f32(l + lsum)
         if v0 > 0 and ref != ref_start:
-            alpha = f32(0.0) if ref_start == -np.inf else _exp2_neg_int(ref - ref_start)
             acc = (acc * alpha).astype(f32)
         acc = (acc + P @ Eq[v0:v0 + tile]).astype(f32)
         if trace is not None:
@@ -105,23 +91,24 @@ def test_online_softmax_row_matches_exact(cdt, kind):
 
 
 def test_rising_logits_exercise_the_rescale():
-    """The rising row moves the reference in most blocks, so the rescale path is what the
+    """The rising row moves the reference in several tiles, so the rescale path is what the
     comparison above checks."""
     t = np.linspace(-30.0, 300.0, 1000)
     moves, ref = 0, -np.inf
-    for c0 in range(0, 1000, 32):
-        cm = t[c0:c0 + 32].max()
-        if cm > ref + 64:
-            moves, ref = moves + 1, (np.ceil(cm) if ref == -np.inf else ref + np.ceil(cm - ref))
-    assert moves >= 4
+    for v0 in range(0, 1000, 192):
+        tm = t[v0:v0 + 192].max()
+        if tm > ref + 64:
+            moves, ref = moves + 1, tm
+    assert moves >= 3
 
 
 @pytest.mark.parametrize("kind", ["rising", "staircase"])
-def test_rescaled_probabilities_keep_one_rounding(kind):
-    """After every rescale inside a tile, each bf16 P value is within one rounding (2^-8
-    relative: half the spacing of 7 stored fraction bits) of the exact 2^(t - ref) for the
-    tile's final reference -- a second rounding could reach about 2^-7.  The staircase puts values just under the margin next to values just
-    over it, so rescaled values stay large."""
+def test_probabilities_carry_one_rounding(kind):
+    """Each bf16 P value is within one rounding (2^-8 relative: half the spacing of 7 stored
+    fraction bits) of the exact 2^(t - ref) for its tile's reference, also where the reference
+    moved inside a tile's columns -- rescaling an already-rounded P by a factor that is not a
+    power of two could reach about 2^-7.  The staircase puts values just under the margin next
+    to values just over it."""
     rng = np.random.default_rng(3)
     V = 960
     if kind == "rising":
@@ -139,3 +126,17 @@ def test_rescaled_probabilities_keep_one_rounding(kind):
         assert err.max() <= 2.0 ** -8 + 1e-6, err.max()
         checked += int(normal.sum())
     assert checked > V // 4
+
+
+@pytest.mark.parametrize("at", [3, 100, 500])
+@pytest.mark.parametrize("cdt", ["bf16", "fp16"])
+def test_dominant_token_is_exact(at, cdt):
+    """A token 1e4 nats above the rest gives P = 1 exactly for it and 0 elsewhere, so O equals
+    its E row exactly (the reference's test_cpu.py:81-88), wherever the token sits."""
+    rng = np.random.default_rng(1)
+    t = rng.normal(0, 1, 700) / LN2
+    t[at] = 1e4 / LN2
+    E = rng.normal(0, 1, (700, 8))
+    O, _ = kernel_row(t, E, cdt)
+    Eq = orc.round_to(E, cdt).astype(np.float32)
+    np.testing.assert_array_equal(O, Eq[at])

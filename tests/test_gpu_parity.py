@@ -543,8 +543,9 @@ def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
 def test_reference_rise_inside_a_tile(dtype):
     """Scores that climb past the forward's emergency margin (64 octaves for bf16, 8 for fp16)
     inside a 192-column tile while the values just under the margin stay significant: the
-    running reference rises by whole octaves and the 16-bit P values already in tensor memory
-    are rescaled by an exact power of two.  Checked against the fp64 oracle."""
+    kernel's first pass over the tile raises the running reference to the tile's max before
+    any P of the tile is written, so no 16-bit P is rescaled.  Checked against the fp64
+    oracle."""
     m = 64.0 if dtype == torch.bfloat16 else 8.0
     N, K, V, D = 130, 64, 1000, 16
     g = torch.Generator().manual_seed(21)
@@ -562,3 +563,14 @@ def test_reference_rise_inside_a_tile(dtype):
     assert torch.isfinite(O).all() and torch.isfinite(lse).all()
     assert rel_err(O, Or) < 2e-2, rel_err(O, Or)
     assert np.abs(npy(lse) - lr).max() < 1e-2
+
+
+@pytest.mark.parametrize("at", [3, 100, 250, 299])
+def test_dominant_token_anywhere_is_exact_in_bf16(at):
+    """test_cpu.py:81-88 with the dominant token (bias 1e4) in any 32-column block of any tile:
+    its P is exactly 1 and every other P is 0, so O == E[at] exactly."""
+    h, W, E, b = make_cpu(K=16, V=300, D=8, dtype=torch.bfloat16)
+    with torch.no_grad():
+        b[at] = 1e4
+    O, _ = swvr.softmax_readout(h, W, E, b)
+    torch.testing.assert_close(O, E[at].to(O.dtype).expand_as(O).detach(), rtol=0, atol=0)
