@@ -177,12 +177,15 @@ static int validate(const swvr_problem* p) {
 }
 
 // ---------------------------------------------------------------------------- forward plan
-// Token tiles per group of the forward's unit order (tc::fwd_unit); SWVR_FWD_GROUP overrides
-// the default.
+// Token tiles per group of the forward's unit order (tc::fwd_unit).  32 keeps about 74 / 32 =
+// 2.3 vocabulary splits streaming at a time on the 74 pairs: measured at c2 (A/B on one B200,
+// two rounds) the forward took 9.6-9.7 ms against 10.1-10.2 ms with every split of a token tile
+// in a row (1) and 10.8 ms with one split for all token tiles (64); 8 and 16 fell in between.
+// SWVR_FWD_GROUP overrides it.
 static int fwd_group(int MT) {
   static const int v = [] {
     const char* s = std::getenv("SWVR_FWD_GROUP");
-    return s ? std::max(1, std::atoi(s)) : 1;
+    return s ? std::max(1, std::atoi(s)) : 32;
   }();
   return std::max(1, std::min(v, std::max(MT, 1)));
 }
