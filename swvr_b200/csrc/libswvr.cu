@@ -3,6 +3,7 @@
 #include "small.cu"
 #include "tc_fwd.cu"
 #include "tc_bwd.cu"
+#include "tc_bwd_stagger.cu"
 #include "tc_gemm.cu"
 #include "abi.cu"
 #include "noalloc.cu"
