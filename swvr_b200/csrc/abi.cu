@@ -284,31 +284,14 @@ static int bwd_aux_loads() {
   return s ? (std::atoi(s) != 0 ? 1 : 0) : 1;
 }
 
-// The staggered score kernel (tc_bwd_stagger.cu) for D <= 64 (1, the default) or 128/192-token
-// tiles (0); SWVR_BWD_STAGGER overrides the default.
-static int bwd_stagger() {
-  const char* s = std::getenv("SWVR_BWD_STAGGER");
-  return s ? (std::atoi(s) != 0 ? 1 : 0) : 0;
-}
-
 // Token splits of the score kernel's units (a 256-row vocabulary tile x a range of token
-// tiles): minimise the rounds over the pairs times a unit's time.  A unit of n tiles takes n
-// tile times; with staggered tiles it takes (n - 1) H + KB stages (H = ceil(KB / 2)), of
-// which the first and last H carry one tile and cost about 0.6 of a two-tile stage.
-static void choose_ts(int VTc, int NT, int sms, bool stagger, int KB, int* TS, int* per_t) {
+// tiles): minimise the rounds over the pairs times the tiles per unit.
+static void choose_ts(int VTc, int NT, int sms, int* TS, int* per_t) {
   int best = 1;
   int64_t best_cost = -1;
   const int tmax = std::max(1, std::min(NT, 32));
-  const int64_t H = (KB + 1) / 2;
   for (int ts = 1; ts <= tmax; ++ts) {
-    const int64_t n = ceil_div(NT, ts);
-    int64_t unit = n;
-    if (stagger) {
-      const int64_t stages = (n - 1) * H + KB;
-      const int64_t single = n == 1 ? stages : std::min<int64_t>(stages, 2 * H);
-      unit = 10 * (stages - single) + 6 * single;
-    }
-    const int64_t cost = ceil_div(static_cast<int64_t>(VTc) * ts, sms) * unit;
+    const int64_t cost = ceil_div(static_cast<int64_t>(VTc) * ts, sms) * ceil_div(NT, ts);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = ts;
@@ -319,8 +302,7 @@ static void choose_ts(int VTc, int NT, int sms, bool stagger, int KB, int* TS, i
 }
 
 struct BwdPlan {
-  int DP, BN, NT, C, sms, KB;
-  bool stagger;
+  int DP, BN, NT, C, sms;
   int64_t Npad;
   bool need_h, need_W, need_E, need_b, need_ds;
   size_t off_delta, off_goc, off_ds, off_dh, off_de, off_db, bytes;
@@ -331,9 +313,7 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   BwdPlan b{};
   b.sms = num_sms();
   b.DP = p.embed_dim <= 64 ? 64 : (p.embed_dim <= 128 ? 128 : 256);
-  b.stagger = b.DP == 64 && bwd_stagger();
-  b.BN = b.stagger ? 128 : tc::bwd_token_tile(b.DP, p.hidden);
-  b.KB = static_cast<int>(ceil_div(p.hidden, 128));
+  b.BN = tc::bwd_token_tile(b.DP, p.hidden);
   b.NT = static_cast<int>(ceil_div(p.n_tokens, b.BN));
   b.Npad = static_cast<int64_t>(b.NT) * b.BN;  // a multiple of 64 (the GEMMs' token K-blocks)
   // The reference's chunk holds chunk x N fp32 scores; dS here is 16-bit, so the same bytes
@@ -356,7 +336,7 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
     if (rows <= 0) continue;
     const int VTc = static_cast<int>(ceil_div(rows, 256));
     int TS, per_t;
-    choose_ts(VTc, b.NT, b.sms / 2, b.stagger, b.KB, &TS, &per_t);
+    choose_ts(VTc, b.NT, b.sms / 2, &TS, &per_t);
     b.max_units = std::max(b.max_units, VTc * TS);
   }
   size_t off = 0;
@@ -414,8 +394,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
   SWVR_TRY(make_map(&sm.w, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 128));
   SWVR_TRY(make_map(&sm.h, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, b.BN / 2));
   SWVR_TRY(make_map(&sm.e, p.E, p.compute_dtype, D, V, p.lde * 2, 64, 128));
-  const int dp_chunk = b.stagger ? tc::kStaggerDpChunk : tc::bwd_dp_chunk(b.BN);
-  SWVR_TRY(make_map(&sm.gok, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, dp_chunk / 2));
+  SWVR_TRY(make_map(&sm.gok, goc, p.compute_dtype, b.DP, N, b.DP * 2, 64, tc::bwd_dp_chunk(b.BN) / 2));
   const int gomw = tc::bwd_gom_width(b.DP);
   SWVR_TRY(make_map(&sm.gom, goc, p.compute_dtype, b.DP, N, b.DP * 2, gomw, b.BN, gomw * 2));
   tc::GemmMaps gm;
@@ -441,7 +420,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     const int rows = static_cast<int>(v1 - v0);
     const int VTc = static_cast<int>(ceil_div(rows, 256));
     int TS, per_t;
-    choose_ts(VTc, b.NT, b.sms / 2, b.stagger, b.KB, &TS, &per_t);
+    choose_ts(VTc, b.NT, b.sms / 2, &TS, &per_t);
     tc::BwdScoresParams sp{};
     sp.N = static_cast<int>(N);
     sp.K = static_cast<int>(K);
@@ -471,10 +450,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     {
       ProfScope ps(kProfBwdScores, st);
       // after the first chunk the previous kernel in the stream is this loop's own
-      if (b.stagger)
-        SWVR_CUDA(tc::launch_bwd_scores_stagger_kernel(bf16, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
-      else
-        SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, b.BN, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
+      SWVR_CUDA(tc::launch_bwd_scores_kernel(bf16, b.DP, b.BN, sm, sp, b.sms / 2, /*pdl=*/v0 > 0, st));
     }
     if (part_de || part_db) {
       void* gE = g.grad_E;

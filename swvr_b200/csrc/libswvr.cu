@@ -3,7 +3,6 @@
 #include "small.cu"
 #include "tc_fwd.cu"
 #include "tc_bwd.cu"
-#include "tc_bwd_stagger.cu"
 #include "tc_gemm.cu"
 #include "abi.cu"
 #include "noalloc.cu"

@@ -95,13 +95,6 @@ int bwd_gom_width(int DP);
 cudaError_t launch_bwd_scores_kernel(bool bf16, int DP, int BN, const BwdScoresMaps& maps,
                                      const BwdScoresParams& prm, int max_pairs, bool pdl, cudaStream_t st);
 
-// The same work with staggered 128-token tiles for D <= 64 (tc_bwd_stagger.cu): two tiles of a
-// unit share every W K-block, dP^T in two 64-token chunks.  Maps as above with BN = 128 and a
-// 64-token dP chunk (gok box {64, 32}).
-cudaError_t launch_bwd_scores_stagger_kernel(bool bf16, const BwdScoresMaps& maps, const BwdScoresParams& prm,
-                                             int max_pairs, bool pdl, cudaStream_t st);
-constexpr int kStaggerDpChunk = 64;
-
 // ------------------------------------------------------------------ backward: dW / dh GEMMs
 struct GemmParams {
   int dw_tiles, dh_tiles;    // number of 256x256 pair tiles of each problem

@@ -366,15 +366,11 @@ def test_masked_vocab_with_neg_inf_bias(dtype):
 
 
 @pytest.mark.parametrize("frozen", ["h", "W", "E", "b", "WE", "hW"])
-@pytest.mark.parametrize("dtype,tile", [(f64, None), (torch.bfloat16, "128"), (torch.bfloat16, "192"),
-                                        (torch.bfloat16, "stagger")])
+@pytest.mark.parametrize("dtype,tile", [(f64, None), (torch.bfloat16, "128"), (torch.bfloat16, "192")])
 def test_frozen_inputs(monkeypatch, frozen, dtype, tile):
     """Frozen inputs skip their work (no dE / db partials, no dS when neither h nor W needs a
-    gradient); bf16 runs both score-tile widths and the staggered tiles."""
-    if tile == "stagger":
-        monkeypatch.setenv("SWVR_BWD_STAGGER", "1")
-    elif tile is not None:
-        monkeypatch.setenv("SWVR_BWD_STAGGER", "0")
+    gradient); bf16 runs both score-tile widths."""
+    if tile is not None:
         monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", tile)
     h, W, E, b = make_cpu(K=16, V=300, D=8, dtype=dtype)
     names = dict(h=h, W=W, E=E, b=b)
@@ -510,7 +506,6 @@ def test_tensor_core_tails(N, K, V, D, dtype):
 def test_backward_192_token_tiles(monkeypatch, N, K, V, D, dtype):
     """192-token score tiles (dP^T in three 64-token chunks), forced on small shapes: a single
     token, ragged last token tiles, vocabulary tails, D below 64."""
-    monkeypatch.setenv("SWVR_BWD_STAGGER", "0")
     monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", "192")
     inputs = make_gpu(N, K, V, D, dtype)
     g = torch.Generator().manual_seed(12)
@@ -529,7 +524,6 @@ def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
     are issued during the next tile's S K-loop).  Both compute the same S, P and dS, and the
     GEMMs only add zero token blocks, so dh and dW agree bit for bit; dE and db sum the same
     terms grouped by different token tiles."""
-    monkeypatch.setenv("SWVR_BWD_STAGGER", "0")
     inputs = make_gpu(N, K, V, D, torch.bfloat16)
     g = torch.Generator().manual_seed(13)
     gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
@@ -543,47 +537,6 @@ def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
     a, b = res["128"], res["192"]
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
     assert rel_err(b[2], a[2]) < 1e-3 and rel_err(b[3], a[3]) < 1e-3
-
-
-@pytest.mark.parametrize("N,K,V,D", [(1, 64, 300, 64), (191, 136, 385, 16), (193, 384, 1000, 64),
-                                     (1000, 1024, 5003, 40), (1300, 2560, 3001, 1), (700, 520, 2000, 64)])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_backward_staggered_tiles(monkeypatch, N, K, V, D, dtype):
-    """The staggered score kernel (two 128-token tiles per W K-block, K loops offset by half a
-    loop) against the fp64 oracle: 1, 2, 3, 5, 8 and 20 K-blocks per tile (odd counts leave
-    one single-tile stage in the middle of a unit), a single token, ragged token and
-    vocabulary tails, D from 1 to 64."""
-    monkeypatch.setenv("SWVR_BWD_STAGGER", "1")
-    inputs = make_gpu(N, K, V, D, dtype)
-    g = torch.Generator().manual_seed(14)
-    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
-    O, lse = swvr.softmax_readout(*inputs, chunk_size=512, logit_scale=0.7)
-    grads = torch.autograd.grad((O * gO).sum() + (lse * glse).sum(), inputs)
-    Or, lr, gr = oracle_eager(*inputs, 0.7, gO, glse)
-    assert rel_err(O, Or) < 2e-2 and np.max(np.abs(npy(lse) - lr)) < 1e-2
-    for n, a, r in zip(["gh", "gW", "gE", "gb"], grads, gr):
-        assert rel_err(a, r) < 2e-2, (n, rel_err(a, r))
-
-
-@pytest.mark.parametrize("N,K,V,D,chunk", [(8192, 1024, 8192, 64, 4096), (3000, 2048, 3001, 40, 8192),
-                                           (5000, 2560, 2000, 64, 1024)])
-def test_backward_staggered_agrees_with_token_tiles(monkeypatch, N, K, V, D, chunk):
-    """Staggered tiles on units of many token tiles (each W K-block shared by two tiles, the
-    deferred dP^T chunks and dE issued between stages) against the 128/192-token tile kernel:
-    the same S, P and dS up to the order of the K-blocks in each tile's fp32 accumulation."""
-    inputs = make_gpu(N, K, V, D, torch.bfloat16)
-    g = torch.Generator().manual_seed(15)
-    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
-    res = {}
-    for st in ("0", "1"):
-        monkeypatch.setenv("SWVR_BWD_STAGGER", st)
-        xs = [x.detach().clone().requires_grad_(True) for x in inputs]
-        O, lse = swvr.softmax_readout(*xs, chunk_size=chunk)
-        torch.autograd.backward([O, lse], [gO, glse])
-        res[st] = [x.grad for x in xs]
-    for name, a, b in zip("hWEb", res["0"], res["1"]):
-        assert torch.isfinite(b).all(), name
-        assert rel_err(b, a) < 2e-3, (name, rel_err(b, a))
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
