@@ -159,6 +159,22 @@ int swvr_bwd_workspace_size(const swvr_problem* p, const swvr_grads* g, size_t* 
 int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The backward in two calls, so that dh can be exchanged while the last dW rows are computed.
+ * No counterpart in the reference (which has no vocabulary sharding); used by the
+ * vocabulary-sharded path to overlap its cross-device dh reduce-scatter with compute.
+ * swvr_bwd_split does the work of swvr_bwd except, on the tensor-core path, the dW rows of the
+ * last vocabulary chunk: dh must go to grad_h_acc (grad_h NULL), and it is final once the
+ * call's work completes on `stream`.  swvr_bwd_finish then computes those dW rows from the
+ * score gradients still in the workspace: same problem, grads and workspace, on a stream
+ * ordered after the split call, before the workspace is reused.  max_sms (0: every SM)
+ * bounds the SMs its kernel occupies, leaving the rest to a collective running beside it.
+ * On the fp32 / fp64 path swvr_bwd_split is swvr_bwd and swvr_bwd_finish does nothing.
+ */
+int swvr_bwd_split(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t workspace_bytes, void* stream);
+int swvr_bwd_finish(const swvr_problem* p, const swvr_grads* g, void* workspace, size_t workspace_bytes,
+                    int32_t max_sms, void* stream);
+
+/*
  * MSE / z-loss / per-token-weight epilogue, forward.  Replaces the loss arithmetic of
  * softmax_readout_mse (swvr/api.py:54-66):
  *   per_tok = mean_d (O - target)^2 + z_loss_weight * LSE^2, times weight[n] if weight;

@@ -67,6 +67,8 @@ _SIGNATURES = {
                              c_void_p, c_void_p]),
     "swvr_bwd_workspace_size": (c_int, [POINTER(Problem), POINTER(Grads), POINTER(c_size_t)]),
     "swvr_bwd": (c_int, [POINTER(Problem), POINTER(Grads), c_void_p, c_size_t, c_void_p]),
+    "swvr_bwd_split": (c_int, [POINTER(Problem), POINTER(Grads), c_void_p, c_size_t, c_void_p]),
+    "swvr_bwd_finish": (c_int, [POINTER(Problem), POINTER(Grads), c_void_p, c_size_t, c_int32, c_void_p]),
     "swvr_mse_fwd": (c_int, [c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_double,
                              c_int32, c_void_p, c_void_p, c_void_p]),
     "swvr_mse_bwd": (c_int, [c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_double,

@@ -356,7 +356,10 @@ static BwdPlan plan_bwd(const swvr_problem& p, const swvr_grads& g) {
   return b;
 }
 
-static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t wsb, cudaStream_t st) {
+// defer_last_dw: leave the dW tiles of the last vocabulary chunk to tc_bwd_finish (dh is final
+// when this call's work completes).
+static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t wsb, cudaStream_t st,
+                  bool defer_last_dw = false) {
   const BwdPlan b = plan_bwd(p, g);
   if (wsb < b.bytes) return fail(SWVR_ERR_WORKSPACE, "backward workspace %zu < required %zu", wsb, b.bytes);
   const int64_t N = p.n_tokens, K = p.hidden, V = p.vocab, D = p.embed_dim;
@@ -464,7 +467,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
       gp.dw_mt = static_cast<int>(ceil_div(rows, 256));
       gp.dw_nt = nt;
       gp.dw_kb = static_cast<int>(b.Npad / 64);
-      gp.dw_tiles = g.grad_W ? gp.dw_mt * nt : 0;
+      gp.dw_tiles = (g.grad_W && !(defer_last_dw && v1 == V)) ? gp.dw_mt * nt : 0;
       gp.dh_mt = static_cast<int>(ceil_div(b.Npad, 256));
       gp.dh_nt = nt;
       gp.dh_kb = static_cast<int>(ceil_div(rows, 64));
@@ -482,6 +485,44 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     ProfScope ps(kProfCast, st);
     SWVR_CUDA(small::cast_f32(dh, g.grad_h, g.grad_h_dtype, N * K, st));
   }
+  return SWVR_OK;
+}
+
+// The dW tiles of the last vocabulary chunk that tc_bwd(..., defer_last_dw) left undone, from the
+// dS still in the workspace, on at most max_pairs CTA pairs.
+static int tc_bwd_finish(const swvr_problem& p, const swvr_grads& g, void* ws, size_t wsb, int max_pairs,
+                         cudaStream_t st) {
+  const BwdPlan b = plan_bwd(p, g);
+  if (wsb < b.bytes) return fail(SWVR_ERR_WORKSPACE, "backward workspace %zu < required %zu", wsb, b.bytes);
+  const int64_t N = p.n_tokens, K = p.hidden, V = p.vocab;
+  if (N == 0 || V == 0 || !g.grad_W) return SWVR_OK;
+  const int64_t v0 = (V - 1) / b.C * b.C;
+  const int rows = static_cast<int>(V - v0);
+  void* ds = static_cast<char*>(ws) + b.off_ds;
+  tc::GemmMaps gm;
+  SWVR_TRY(make_map(&gm.ds_k, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 128));
+  SWVR_TRY(make_map(&gm.ds_mn, ds, p.compute_dtype, b.Npad, rows, b.Npad * 2, 64, 64));
+  SWVR_TRY(make_map(&gm.h_mn, p.h, p.compute_dtype, K, N, p.ldh * 2, 64, 64));
+  SWVR_TRY(make_map(&gm.w_mn, p.W, p.compute_dtype, K, V, p.ldw * 2, 64, 64));
+  if (g.grad_W_dtype == SWVR_F32)
+    SWVR_TRY(make_map(&gm.gw, g.grad_W, SWVR_F32, K, V, g.ld_grad_W * 4, 32, 128));
+  else
+    SWVR_TRY(make_map(&gm.gw, g.grad_W, p.compute_dtype, K, V, g.ld_grad_W * 2, 64, 128));
+  gm.dh = gm.w_mn;  // no dh tiles
+  tc::GemmParams gp{};
+  const int nt = static_cast<int>(ceil_div(K, 256));
+  gp.dw_mt = static_cast<int>(ceil_div(rows, 256));
+  gp.dw_nt = nt;
+  gp.dw_kb = static_cast<int>(b.Npad / 64);
+  gp.dw_tiles = gp.dw_mt * nt;
+  gp.dh_tiles = 0;
+  gp.dh_mt = gp.dh_nt = 1;
+  gp.dh_kb = 1;
+  gp.v_begin = static_cast<int>(v0);
+  gp.gw_f32 = g.grad_W_dtype == SWVR_F32 ? 1 : 0;
+  const int pairs = max_pairs > 0 ? std::min(max_pairs, b.sms / 2) : b.sms / 2;
+  ProfScope ps(kProfGemm, st);
+  SWVR_CUDA(tc::launch_gemm_kernel(p.compute_dtype == SWVR_BF16, gm, gp, pairs, /*pdl=*/false, st));
   return SWVR_OK;
 }
 
@@ -613,6 +654,25 @@ int swvr_bwd(const swvr_problem* p, const swvr_grads* g, void* ws, size_t wsb, v
   return simt::bwd(*p, *g, ws, st) == SWVR_OK
              ? SWVR_OK
              : fail(SWVR_ERR_CUDA, "SIMT backward launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+}
+
+int swvr_bwd_split(const swvr_problem* p, const swvr_grads* g, void* ws, size_t wsb, void* stream) {
+  SWVR_TRY(validate(p));
+  if (!g) return fail(SWVR_ERR_INVALID_ARGUMENT, "grads is NULL");
+  if (p->n_tokens > 0 && (!g->grad_O || !g->grad_lse || !g->O || !g->lse))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL backward input");
+  if (g->grad_h) return fail(SWVR_ERR_INVALID_ARGUMENT, "swvr_bwd_split leaves dh un-cast: pass grad_h_acc, not grad_h");
+  if (!is_tc(p->compute_dtype)) return swvr_bwd(p, g, ws, wsb, stream);  // nothing deferred
+  return tc_bwd(*p, *g, ws, wsb, static_cast<cudaStream_t>(stream), /*defer_last_dw=*/true);
+}
+
+int swvr_bwd_finish(const swvr_problem* p, const swvr_grads* g, void* ws, size_t wsb, int32_t max_sms,
+                    void* stream) {
+  SWVR_TRY(validate(p));
+  if (!g) return fail(SWVR_ERR_INVALID_ARGUMENT, "grads is NULL");
+  if (max_sms < 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "max_sms must be >= 0");
+  if (!is_tc(p->compute_dtype)) return SWVR_OK;
+  return tc_bwd_finish(*p, *g, ws, wsb, max_sms / 2, static_cast<cudaStream_t>(stream));
 }
 
 int swvr_mse_fwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void* O, const void* lse,

@@ -239,39 +239,50 @@ def _grad_buffer(x: torch.Tensor, cdt: torch.dtype, tc: bool) -> Tuple[torch.Ten
 
 
 def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b,
-              dh_partial=False):
+              dh_partial=False, split=False):
     """Gradients of one readout.  With ``dh_partial`` the first result is dh un-cast, in the
     accumulation dtype (a vocabulary shard's contribution, summed across shards by the caller)
-    instead of dh in h's dtype."""
+    instead of dh in h's dtype.  With ``split`` (and ``dh_partial``) a fifth result is returned:
+    None, or a function ``finish(max_sms)`` that must be called, after this call and before
+    gW is read, to compute the dW rows of the last vocabulary chunk (``swvr_bwd_split`` /
+    ``swvr_bwd_finish``): dh is final on the current stream as soon as this call returns, so
+    its cross-device exchange can run beside the finish kernel."""
+    res = _backward_impl(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b,
+                         dh_partial, split and dh_partial)
+    return res if split else res[:4]
+
+
+def _backward_impl(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W, need_E, need_b,
+                   dh_partial, split):
     dev = _require_cuda(h, W, E, bias, gO, glse, O, lse)
     adt = O.dtype
     N, K, V, D = h.shape[0], h.shape[1], W.shape[0], E.shape[1]
     cdt = _engine_dtype(cdt, D)
     tc = _tensor_core(cdt)
     need_b = need_b and bias is not None
-    if dh_partial:
-        gh = torch.zeros(N, K, dtype=adt, device=dev) if need_h else None
+    if dh_partial:  # the library overwrites it (accumulate_grad_h = 0); the V == 0 / N == 0 paths zero it
+        gh = torch.empty(N, K, dtype=adt, device=dev) if need_h else None
     else:
         gh = torch.empty(h.shape, dtype=h.dtype, device=dev) if need_h else None
     gW_buf, gW = _grad_buffer(W, cdt, tc) if need_W else (None, None)
     gE = torch.empty(E.shape, dtype=E.dtype, device=dev) if need_E else None
     gb = torch.empty(bias.shape, dtype=bias.dtype, device=dev) if need_b else None
     if not (need_h or need_W or need_E or need_b):
-        return gh, gW, gE, gb
+        return gh, gW, gE, gb, None
     if V == 0 or N == 0:
         for x in (gh, gW, gE, gb):
             if x is not None:
                 x.zero_()
-        return gh, gW, gE, gb
+        return gh, gW, gE, gb, None
     if _param_cast_chunks(W, E, cdt):
-        return _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb,
-                                    dev)
+        return (*_backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE,
+                                      gb, dev), None)
     hc, Wc, Ec, b = _prepare(h, W, E, bias, cdt)
     K8 = hc.shape[1]
     padded_k = K8 != K
     gh_buf = gh
     if need_h and padded_k:
-        gh_buf = torch.zeros(N, K8, dtype=gh.dtype, device=dev)
+        gh_buf = torch.empty(N, K8, dtype=gh.dtype, device=dev)
     if need_W and padded_k:
         gW_buf = torch.empty(V, K8, dtype=gW_buf.dtype, device=dev)
     p = _problem(hc, Wc, Ec, b, logit_scale, chunk, cdt)
@@ -292,15 +303,34 @@ def _backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, 
         g.grad_bias, g.grad_bias_dtype = gb.data_ptr(), nat.dtype_code(gb.dtype)
     lib = nat.lib()
     nbytes = nat.c_size_t(0)
+    split = split and need_W and _tensor_core(cdt)
     with torch.cuda.device(dev):
         nat.check(lib.swvr_bwd_workspace_size(p, g, nat.ctypes.byref(nbytes)), "swvr_bwd_workspace_size")
         ws = _workspace(nbytes.value, dev)
-        nat.check(lib.swvr_bwd(p, g, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)), "swvr_bwd")
+        call = lib.swvr_bwd_split if split else lib.swvr_bwd
+        nat.check(call(p, g, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)), "swvr_bwd_split" if split else "swvr_bwd")
     if need_h and gh_buf is not gh:
         gh.copy_(gh_buf[:, :K])
-    if need_W and gW_buf is not gW:
-        gW.copy_(gW_buf[:, :K])
-    return gh, gW, gE, gb
+
+    def finish_w():
+        if need_W and gW_buf is not gW:
+            gW.copy_(gW_buf[:, :K])
+
+    if not split:
+        finish_w()
+        return gh, gW, gE, gb, None
+
+    keep = (hc, Wc, Ec, b, gO, glse)  # the struct holds raw pointers into these
+
+    def finish(max_sms=0):
+        # the operand copies, grads struct and workspace stay referenced by this closure until
+        # the finish kernel has been issued on the same stream
+        assert keep is not None
+        with torch.cuda.device(dev):
+            nat.check(lib.swvr_bwd_finish(p, g, ws.data_ptr(), ws.numel(), int(max_sms), nat.stream_ptr(dev)),
+                      "swvr_bwd_finish")
+        finish_w()
+    return gh, gW, gE, gb, finish
 
 
 def _backward_param_cast(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, gh, gW_buf, gW, gE, gb, dev):

@@ -12,12 +12,15 @@ backward  every rank gets the same (dO, dLSE) because the loss is computed on th
           replicated O, LSE; it runs the fused backward over its shard (dW, dE, db are
           local and final) and accumulates its partial dh in fp32; a reduce-scatter (SUM)
           of dh [N, K] fp32 and an all-gather of the slabs cast to h's dtype finish dh.
+          The reduce-scatter starts as soon as dh is final: the dW rows of the shard's last
+          vocabulary chunk are computed beside it (``swvr_bwd_split`` / ``swvr_bwd_finish``).
 
 The compute backend is pluggable so the collective logic can be exercised on CPU ``gloo``
 ranks in tests; the default is libswvr_b200.so and nothing else runs in production.
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional, Tuple
 
 import torch
@@ -59,9 +62,11 @@ class NativeBackend:
 
     @staticmethod
     def backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_h, need_W, need_E, need_b):
-        """(this shard's dh in the accumulation dtype or None, gW, gE, gb)."""
+        """(this shard's dh in the accumulation dtype or None, gW, gE, gb, finish): ``finish`` is
+        None or a function ``finish(max_sms)`` computing the last vocabulary chunk's dW rows,
+        which may run beside the dh exchange (dh is final before it)."""
         return _backward(gO, glse, h, W, E, bias, O, lse, scale, chunk, cdt, need_h, need_W, need_E, need_b,
-                         dh_partial=True)
+                         dh_partial=True, split=True)
 
 
 _BACKEND = NativeBackend
@@ -81,19 +86,31 @@ def _resolve(group_name: str):
     return dist.distributed_c10d._resolve_process_group(group_name)
 
 
-def _sum_dh_over_shards(dh: torch.Tensor, out_dtype: torch.dtype, group) -> torch.Tensor:
+def comm_sms() -> int:
+    """SMs left free for the dh reduce-scatter while the last dW rows are computed beside it
+    (env ``SWVR_VP_COMM_SMS``, default 16; 0 gives the finish kernel every SM)."""
+    return max(0, int(os.environ.get("SWVR_VP_COMM_SMS", "16")))
+
+
+def _sum_dh_over_shards(dh: torch.Tensor, out_dtype: torch.dtype, group, finish=None) -> torch.Tensor:
     """The sum over ranks of the shards' dh partials, in ``out_dtype`` on every rank.
 
     A reduce-scatter in the accumulation dtype (each rank sums one slab of rows, in a fixed
     order) followed by an all-gather of the slabs already cast to h's dtype: the same fp32
-    sum as an all-reduce, with 3/4 of its traffic for a 16-bit h."""
+    sum as an all-reduce, with 3/4 of its traffic for a 16-bit h.  ``finish`` (the deferred
+    last dW rows, see NativeBackend.backward) runs on the current stream while the
+    reduce-scatter runs on the process group's stream."""
     world = dist.get_world_size(group)
     N, K = dh.shape
     rows = -(-N // world)
     if rows * world != N:
         dh = torch.nn.functional.pad(dh, (0, 0, 0, rows * world - N))
     slab = torch.empty(rows, K, dtype=dh.dtype, device=dh.device)
-    dist.reduce_scatter_tensor(slab, dh.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    work = dist.reduce_scatter_tensor(slab, dh.contiguous(), op=dist.ReduceOp.SUM, group=group, async_op=True)
+    if finish is not None:
+        sms = torch.cuda.get_device_properties(dh.device).multi_processor_count if dh.is_cuda else 0
+        finish(max(2, sms - comm_sms()) if comm_sms() else 0)
+    work.wait()
     full = torch.empty(rows * world, K, dtype=out_dtype, device=dh.device)
     dist.all_gather_into_tensor(full, slab.to(out_dtype), group=group)
     return full[:N]
@@ -132,9 +149,14 @@ def _vp_bwd_op(gO: torch.Tensor, glse: torch.Tensor, h: torch.Tensor, W: torch.T
                cdt: torch.dtype, group_name: str, need_h: bool, need_W: bool, need_E: bool,
                need_b: bool) -> List[torch.Tensor]:
     group = _resolve(group_name)
-    dh, gW, gE, gb = _BACKEND.backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h, need_W,
-                                       need_E, need_b)
-    gh = _sum_dh_over_shards(dh, h.dtype, group) if need_h else None
+    dh, gW, gE, gb, finish = _BACKEND.backward(gO, glse, h, W, E, bias, O, lse, logit_scale, chunk, cdt, need_h,
+                                               need_W, need_E, need_b)
+    if need_h:
+        gh = _sum_dh_over_shards(dh, h.dtype, group, finish)
+    else:
+        gh = None
+        if finish is not None:
+            finish(0)
     return [x if x is not None else h.new_empty(0) for x in (gh, gW, gE, gb)]
 
 

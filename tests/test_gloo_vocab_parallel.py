@@ -47,7 +47,7 @@ class OracleBackend:
                                               E.detach().numpy(), b, O.numpy(), lse.numpy(), scale, chunk, "fp64",
                                               need_h, need_W, need_E, need_b)
         t = lambda x: None if x is None else torch.from_numpy(np.ascontiguousarray(x))
-        return t(gh), t(gW), t(gE), t(gb)
+        return t(gh), t(gW), t(gE), t(gb), None
 
 
 def _inputs(N=7, K=12, V=41, D=5):

@@ -126,11 +126,45 @@ def test_sharded_compute_on_one_gpu(G):
     dh = torch.zeros(N, K, dtype=torch.float32, device="cuda")
     gW, gE, gb = [], [], []
     for a, z in spans:
-        d, x, y, c = vp.NativeBackend.backward(gO, glse, h, W[a:z], E[a:z], b[a:z], O, lse, 1.0, 4096, cdt,
-                                               True, True, True, True)
+        d, x, y, c, finish = vp.NativeBackend.backward(gO, glse, h, W[a:z], E[a:z], b[a:z], O, lse, 1.0, 4096, cdt,
+                                                       True, True, True, True)
+        finish(16)  # the last chunk's dW rows on a bounded set of SMs
         assert d.dtype == torch.float32 and d.shape == (N, K)
         dh += d
         gW.append(x), gE.append(y), gb.append(c)
     gr = orc.readout_grads(npy(h), npy(W), npy(E), npy(b), npy(gO), npy(glse))
     for name, got, ref in zip("hWEb", [dh, torch.cat(gW), torch.cat(gE), torch.cat(gb)], gr):
         assert rel_err(got, ref) < 2e-2, (name, rel_err(got, ref))
+
+
+@pytest.mark.parametrize("K,max_sms", [(512, 0), (300, 16), (1024, 132)])
+def test_split_backward_equals_one_call(K, max_sms):
+    """swvr_bwd_split + swvr_bwd_finish (the last vocabulary chunk's dW rows computed later, on a
+    bounded set of SMs) give bit for bit the gradients of one swvr_bwd call: the same kernels
+    compute the same tiles.  K = 300 takes the zero-padded K path."""
+    from swvr_b200.ops import _backward
+
+    N_, V_, D_ = 700, 9000, 64
+    h, W, E, b = (x.detach() for x in make_inputs_gpu(N_, K, V_, D_))
+    g = torch.Generator().manual_seed(3)
+    gO = (0.02 * torch.randn(N_, D_, generator=g)).cuda()
+    glse = (0.01 * torch.randn(N_, generator=g)).cuda()
+    from swvr_b200 import softmax_readout
+    O, lse = softmax_readout(h, W, E, b, chunk_size=2048)
+    args = (gO, glse, h, W, E, b, O, lse, 1.0, 2048, torch.bfloat16, True, True, True, True)
+    ref = _backward(*args, dh_partial=True)
+    dh, gW, gE, gb, finish = _backward(*args, dh_partial=True, split=True)
+    assert finish is not None
+    finish(max_sms)
+    torch.cuda.synchronize()
+    for name, a, r in zip(("dh", "gW", "gE", "gb"), (dh, gW, gE, gb), ref):
+        assert torch.equal(a, r), name
+
+
+def make_inputs_gpu(N_, K, V_, D_):
+    g = torch.Generator().manual_seed(8)
+    h = torch.randn(N_, K, generator=g).to(torch.bfloat16).cuda()
+    W = (K ** -0.5 * torch.randn(V_, K, generator=g)).to(torch.bfloat16).cuda()
+    E = (0.02 * torch.randn(V_, D_, generator=g)).to(torch.bfloat16).cuda()
+    b = (0.02 * torch.randn(V_, generator=g)).to(torch.bfloat16).cuda()
+    return h, W, E, b
