@@ -57,7 +57,14 @@ CONFIGS = {
     "c4": dict(N=131072, K=4096, V=152064, D=64, bias=True, weight=None, z=0.0, lead=(32, 4096), checkpoint=True),
     # profiling size for ncu --set full captures: the c2 kernels on a cut (W 168 MB > L2)
     "prof": dict(N=4096, K=2560, V=32768, D=64, bias=True, weight=0.9, z=1e-4),
+    # fp32 operands (exact path: CUDA-core SIMT kernels here, cuBLAS fp32 without TF32 in the
+    # reference) at a mid size, to compare the two fp32 paths on one box
+    "fp32": dict(N=4096, K=1024, V=32768, D=64, bias=True, weight=0.9, z=1e-4, dtype="fp32"),
 }
+
+
+def param_dtype(c):
+    return torch.float32 if c.get("dtype") == "fp32" else torch.bfloat16
 
 
 def metric_name(args, c):
@@ -228,12 +235,13 @@ def make_inputs(c, device, rank, world):
     N, K, V, D = c["N"], c["K"], c["V"], c["D"]
     lead = tuple(c.get("lead") or (N,))
     v0, v1 = shard_range(V, world, rank)
+    dt = param_dtype(c)
     g = torch.Generator(device=device).manual_seed(1234)
-    W_full = (K ** -0.5 * torch.randn(V, K, generator=g, device=device)).to(torch.bfloat16)
-    E_full = (0.02 * torch.randn(V, D, generator=g, device=device)).to(torch.bfloat16)
-    b_full = (0.02 * torch.randn(V, generator=g, device=device)).to(torch.bfloat16) if c["bias"] else None
+    W_full = (K ** -0.5 * torch.randn(V, K, generator=g, device=device)).to(dt)
+    E_full = (0.02 * torch.randn(V, D, generator=g, device=device)).to(dt)
+    b_full = (0.02 * torch.randn(V, generator=g, device=device)).to(dt) if c["bias"] else None
     gs = torch.Generator(device=device).manual_seed(99)
-    h = torch.randn(N, K, generator=gs, device=device).to(torch.bfloat16).view(*lead, K)
+    h = torch.randn(N, K, generator=gs, device=device).to(dt).view(*lead, K)
     if c.get("target") == "erows":
         ids = torch.randint(0, V, (N,), generator=gs, device=device)
         t = E_full[ids].float() + 0.01 * torch.randn(N, D, generator=gs, device=device)
@@ -495,10 +503,11 @@ class CpuSample:
         N, K, D = c["N"], c["K"], c["D"]
         lead = tuple(c.get("lead") or (N,))
         g = torch.Generator().manual_seed(0)
-        self.h = torch.randn(N, K, generator=g).to(torch.bfloat16).view(*lead, K)
-        self.W = (K ** -0.5 * torch.randn(rows, K, generator=g)).to(torch.bfloat16)
-        self.E = (0.02 * torch.randn(rows, D, generator=g)).to(torch.bfloat16)
-        self.b = (0.02 * torch.randn(rows, generator=g)).to(torch.bfloat16) if c["bias"] else None
+        dt = param_dtype(c)
+        self.h = torch.randn(N, K, generator=g).to(dt).view(*lead, K)
+        self.W = (K ** -0.5 * torch.randn(rows, K, generator=g)).to(dt)
+        self.E = (0.02 * torch.randn(rows, D, generator=g)).to(dt)
+        self.b = (0.02 * torch.randn(rows, generator=g)).to(dt) if c["bias"] else None
         if c.get("target") == "erows":
             ids = torch.randint(0, rows, (N,), generator=g)
             self.t = (self.E[ids].float() + 0.01 * torch.randn(N, D, generator=g)).view(*lead, D)
@@ -513,7 +522,8 @@ class CpuSample:
                else "the numpy restatement of swvr's chunked path (oracle/swvr_oracle.py; the reference "
                     "install was not found)")
         return (f"vocabulary slice of {self.rows} of {c['V']} rows against all N={c['N']} tokens "
-                f"(K={c['K']}, D={c['D']}), bf16 inputs, chunk 8192, fwd+bwd+loss: {src}; "
+                f"(K={c['K']}, D={c['D']}), {'fp32' if c.get('dtype') == 'fp32' else 'bf16'} inputs, chunk 8192, "
+                f"fwd+bwd+loss: {src}; "
                 f"{self.threads} threads")
 
     def run(self):
@@ -543,11 +553,12 @@ class CpuSample:
         h, W, E, b, t = f(self.h), f(self.W), f(self.E), f(self.b), f(self.t)
         w = None if self.w is None else self.w.numpy().reshape(-1)
         t0 = time.perf_counter()
-        O, lse = orc.chunked_forward(h, W, E, b, 1.0, 8192, "bf16")
+        cdt = "fp32" if c.get("dtype") == "fp32" else "bf16"
+        O, lse = orc.chunked_forward(h, W, E, b, 1.0, 8192, cdt)
         z = 0.0 if c.get("raw") else c["z"]
         orc.mse_forward(O, lse, t, w, "mean", z)
         gO, glse, _, _ = orc.mse_backward(O, lse, t, w, "mean", z)
-        orc.chunked_backward(gO, glse, h, W, E, b, O, lse, 1.0, 8192, "bf16")
+        orc.chunked_backward(gO, glse, h, W, E, b, O, lse, 1.0, 8192, cdt)
         return time.perf_counter() - t0
 
 
@@ -580,7 +591,7 @@ def run_reference_arm(args, c, rank, world):
         "ms_per_step_scope": "one step = one bounded sample (cpu_baseline.sample); a whole-vocabulary step "
                              f"would take about {sec * c['V'] / smp.rows:.0f} s",
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16 inputs, fp32 CPU math", "data": "synthetic",
+        "dtype": ("fp32" if c.get("dtype") == "fp32" else "bf16 inputs") + ", fp32 CPU math", "data": "synthetic",
         "config": config_dict(args, c, 1),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                          "kind": smp.kind, "sample": smp.describe()},
@@ -669,7 +680,7 @@ def main():
             "metric": metric_name(args, c),
             "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(r["ms"], 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32" if c.get("dtype") == "fp32" else "bf16",
             "data": "synthetic (seeded; BASELINE config distributions; one problem at every N)",
             "config": config_dict(args, c, world),
             "tflops_exec": round(f_exec(c) / (r["ms"] * 1e-3) / 1e12, 2),
