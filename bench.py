@@ -120,7 +120,7 @@ def load_peaks():
 #       python bench.py --steps 2 --warmup 3 --no-cpu-baseline --no-reference-gpu
 # Other configs, chunk sizes or GPU counts report null.
 CAPTURED_TRAFFIC_GB = {("c2", "gemm_kernel"): 2.956, ("c2", "bwd_scores_kernel"): 1.376,
-                       ("c2", "fwd_kernel"): 10.531}
+                       ("c2", "fwd_kernel"): 3.259}
 
 
 def load_reference():

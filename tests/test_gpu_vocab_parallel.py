@@ -47,8 +47,17 @@ def _worker(rank, world, port, out_dir):
     loss = vp.softmax_readout_mse_vocab_parallel(hh, Ws, Es, t, bs, weight=w, z_loss_weight=1e-4, chunk_size=4096)
     loss.backward()
     O, lse = vp.softmax_readout_vocab_parallel(h, Ws.detach(), Es.detach(), bs.detach(), chunk_size=4096)
+    # the same step under activation checkpointing and under torch.compile(fullgraph=True)
+    def step(x, Wp, Ep, bp):
+        return vp.softmax_readout_mse_vocab_parallel(x, Wp, Ep, t, bp, weight=w, z_loss_weight=1e-4, chunk_size=4096)
+    extra = {}
+    for mode, fn in (("ckpt", lambda *a: torch.utils.checkpoint.checkpoint(step, *a, use_reentrant=False)),
+                     ("comp", torch.compile(step, fullgraph=True))):
+        xs = [hh.detach().clone().requires_grad_(True)] + [x.detach().clone().requires_grad_(True) for x in (Ws, Es, bs)]
+        fn(*xs).backward()
+        extra.update({f"{mode}_{k}": x.grad.float().cpu().numpy() for k, x in zip("hWEb", xs)})
     torch.cuda.synchronize()
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), loss=loss.item(), O=O.float().cpu().numpy(),
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **extra, loss=loss.item(), O=O.float().cpu().numpy(),
              lse=lse.float().cpu().numpy(), gh=hh.grad.float().cpu().numpy(), gW=Ws.grad.float().cpu().numpy(),
              gE=Es.grad.float().cpu().numpy(), gb=bs.grad.float().cpu().numpy(), v0=v0, v1=v1)
     dist.barrier()
@@ -93,6 +102,9 @@ def test_two_gpu_vocab_parallel_matches_single_gpu(tmp_path):
         assert rel_err(torch.from_numpy(z["gW"]), Wf.grad[v0:v1]) < 2e-2
         assert rel_err(torch.from_numpy(z["gE"]), Ef.grad[v0:v1]) < 2e-2
         assert rel_err(torch.from_numpy(z["gb"]), bf.grad[v0:v1]) < 2e-2
+        for mode in ("ckpt", "comp"):  # checkpointing and torch.compile give the plain step's gradients
+            for k in "hWEb":
+                assert rel_err(torch.from_numpy(z[f"{mode}_{k}"]), torch.from_numpy(z[f"g{k}"])) < 1e-6, (mode, k)
 
 
 @pytest.mark.parametrize("G", [2, 3, 8])
