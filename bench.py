@@ -386,27 +386,52 @@ def run_ours(args, c, rank, world, device):
         h2d = -(-h2d // world)
 
     def e2e_step():
-        if world > 1:
-            hd = vp.replicate_from_host(h_host, device)
-            td = vp.replicate_from_host(t_host, device)
-            wd = vp.replicate_from_host(w_host, device) if w_host is not None else None
-        else:
-            h_dev.copy_(h_host, non_blocking=True)
-            t_dev.copy_(t_host, non_blocking=True)
-            if w_dev is not None:
-                w_dev.copy_(w_host, non_blocking=True)
-            hd, td, wd = h_dev, t_dev, w_dev
-        hh = hd.detach().requires_grad_(True)
-        loss = step(hh, td, wd)
+        hd = vp.replicate_from_host(h_host, device)
+        td = vp.replicate_from_host(t_host, device)
+        wd = vp.replicate_from_host(w_host, device) if w_host is not None else None
+        loss = step(hd.detach().requires_grad_(True), td, wd)
         loss_host.copy_(loss.detach(), non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
+    # One GPU: the inputs are double-buffered and step i + 1's are copied on a side stream while
+    # step i computes (as a training loop prefetches its next batch); every copy, the first
+    # included, runs inside the timed region.
+    copy_stream = torch.cuda.Stream(device)
+    bufs = [(h_dev, t_dev, w_dev), (torch.empty_like(h_dev), torch.empty_like(t_dev),
+                                     torch.empty_like(w_dev) if w_dev is not None else None)]
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    consumed = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def issue_copy(i):
+        hb, tb, wb = bufs[i % 2]
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(consumed[i % 2])  # the step that last read this buffer is done
+            hb.copy_(h_host, non_blocking=True)
+            tb.copy_(t_host, non_blocking=True)
+            if wb is not None:
+                wb.copy_(w_host, non_blocking=True)
+            copied[i % 2].record(copy_stream)
+
+    def e2e_run(n):
+        if world > 1:
+            for _ in range(n):
+                e2e_step()
+            return
+        copy_stream.wait_stream(stream)
+        issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            stream.wait_event(copied[i % 2])
+            hb, tb, wb = bufs[i % 2]
+            loss = step(hb.detach().requires_grad_(True), tb, wb)
+            loss_host.copy_(loss.detach(), non_blocking=True)
+            consumed[i % 2].record(stream)
+
+    e2e_run(2)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_run(args.steps)
     e1.record(stream)
     barrier()
     ms_e2e = e0.elapsed_time(e1) / args.steps
@@ -702,7 +727,9 @@ def main():
                     "ms_per_step": round(r["ms_e2e"], 3), "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": 4,
                     "h2d_scope": ("per rank: each rank copies 1/N of the replicated h, target and weight from pinned "
                                   "host memory and NVLink all-gathers the rest (vocab_parallel.replicate_from_host)"
-                                  if world > 1 else "whole job")},
+                                  if world > 1 else "whole job: pinned host buffers, double-buffered on the device; step "
+                                  "i+1's inputs are copied on a side stream while step i computes, every copy inside "
+                                  "the timed region")},
         }
         if ref_gpu is not None:
             if "unavailable" not in ref_gpu:

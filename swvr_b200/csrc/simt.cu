@@ -12,31 +12,50 @@ namespace simt {
 
 // C[m, n] = alpha * sum_k A[m, k] B[k, n] + beta * C[m, n] with arbitrary strides (the callers
 // pass transposes as strides) and C of any dtype.  128 x 128 block tiles, 8-deep K steps,
-// 8 x 8 outputs per thread; the next K step's tiles are fetched into registers while the
-// current one is multiplied.  Global loads run along whichever dimension of A / B has unit
-// stride, so they coalesce for row- and column-major operands alike.
+// 8 x 8 outputs per thread.  The block tiles are double-buffered in shared memory (one barrier
+// per K step) and the next K step's tiles are fetched into registers while the current one is
+// multiplied.  Global loads run along whichever dimension of A / B has unit stride, so they
+// coalesce for row- and column-major operands alike, 16 bytes at a time where the layout allows
+// it; the fp32 kernel reads its fragments from shared memory 16 bytes at a time.
 constexpr int BM = 128, BN = 128, BK = 8, PAD = 4;
 
 template <typename T>
 struct GemmTileLoader {
   // one thread's 4 elements of the BM x BK tile of A and of the BK x BN tile of B
   T a[4], b[4];
+  // vec_a / vec_b: the 4 elements are contiguous, 16-byte aligned and all in or all out of range
   __device__ __forceinline__ void load(const T* __restrict__ A, int64_t sam, int64_t sak, const T* __restrict__ B,
                                        int64_t sbk, int64_t sbn, int64_t M, int64_t N, int64_t K, int64_t m0,
-                                       int64_t n0, int64_t k0, int t) {
+                                       int64_t n0, int64_t k0, int t, bool vec_a, bool vec_b) {
+    if (vec_a) {
+      const int64_t m = sak == 1 ? m0 + t / 2 : m0 + (t % 32) * 4;
+      const int64_t k = sak == 1 ? k0 + (t % 2) * 4 : k0 + t / 32;
+      const bool in = sak == 1 ? (m < M && k < K) : (m < M && k < K);
+      const float4 v = in ? *reinterpret_cast<const float4*>(A + m * sam + k * sak) : make_float4(0.f, 0.f, 0.f, 0.f);
+      a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
+    } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int64_t m, k;
-      if (sak == 1) { m = m0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous in A
-      else          { m = m0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // M contiguous (or general)
-      a[e] = (m < M && k < K) ? A[m * sam + k * sak] : T(0);
+      for (int e = 0; e < 4; ++e) {
+        int64_t m, k;
+        if (sak == 1) { m = m0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous in A
+        else          { m = m0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // M contiguous (or general)
+        a[e] = (m < M && k < K) ? A[m * sam + k * sak] : T(0);
+      }
     }
+    if (vec_b) {
+      const int64_t n = sbn == 1 ? n0 + (t % 32) * 4 : n0 + t / 2;
+      const int64_t k = sbn == 1 ? k0 + t / 32 : k0 + (t % 2) * 4;
+      const bool in = n < N && k < K;
+      const float4 v = in ? *reinterpret_cast<const float4*>(B + k * sbk + n * sbn) : make_float4(0.f, 0.f, 0.f, 0.f);
+      b[0] = v.x, b[1] = v.y, b[2] = v.z, b[3] = v.w;
+    } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int64_t n, k;
-      if (sbn == 1) { n = n0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // N contiguous in B
-      else          { n = n0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous (or general)
-      b[e] = (n < N && k < K) ? B[k * sbk + n * sbn] : T(0);
+      for (int e = 0; e < 4; ++e) {
+        int64_t n, k;
+        if (sbn == 1) { n = n0 + (t % 32) * 4 + e; k = k0 + t / 32; }  // N contiguous in B
+        else          { n = n0 + t / 2; k = k0 + (t % 2) * 4 + e; }   // K contiguous (or general)
+        b[e] = (n < N && k < K) ? B[k * sbk + n * sbn] : T(0);
+      }
     }
   }
   __device__ __forceinline__ void store(T (*As)[BM + PAD], T (*Bs)[BN + PAD], bool a_kcontig, bool b_ncontig,
@@ -51,12 +70,34 @@ struct GemmTileLoader {
   }
 };
 
+// Four consecutive elements of a shared-memory row (16-byte aligned for fp32).
+template <typename T>
+__device__ __forceinline__ void frag4(const T* p, T* out) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    out[0] = v.x, out[1] = v.y, out[2] = v.z, out[3] = v.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = p[i];
+  }
+}
+
+// True when the loader's 4 elements along the unit-stride dimension form an aligned float4
+// that is either wholly inside or wholly outside the extent: fp32, 16-byte aligned base,
+// the other stride and the unit-stride extent multiples of 4.
+template <typename T>
+static bool vec4_ok(const T* p, int64_t s_other, int64_t s_unit, int64_t unit_extent) {
+  return sizeof(T) == 4 && s_unit == 1 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && s_other % 4 == 0 &&
+         unit_extent % 4 == 0;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_kernel(int64_t M, int64_t N, int64_t K, T alpha, const T* __restrict__ A,
                                                    int64_t sam, int64_t sak, const T* __restrict__ B, int64_t sbk,
-                                                   int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn) {
-  __shared__ __align__(16) T As[BK][BM + PAD];
-  __shared__ __align__(16) T Bs[BK][BN + PAD];
+                                                   int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn,
+                                                   bool vec_a, bool vec_b) {
+  __shared__ __align__(16) T As[2][BK][BM + PAD];
+  __shared__ __align__(16) T Bs[2][BK][BN + PAD];
   const int t = threadIdx.x, tx = t % 16, ty = t / 16;
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM, n0 = static_cast<int64_t>(blockIdx.x) * BN;
   const bool a_kcontig = sak == 1, b_ncontig = sbn == 1;
@@ -66,28 +107,29 @@ __global__ void __launch_bounds__(256) gemm_kernel(int64_t M, int64_t N, int64_t
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = T(0);
   GemmTileLoader<T> ld;
-  ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, 0, t);
+  ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, 0, t, vec_a, vec_b);
+  ld.store(As[0], Bs[0], a_kcontig, b_ncontig, t);
+  __syncthreads();
+  int cur = 0;
   for (int64_t k0 = 0; k0 < K; k0 += BK) {
-    __syncthreads();  // the previous step's reads of As / Bs are done
-    ld.store(As, Bs, a_kcontig, b_ncontig, t);
-    __syncthreads();
-    if (k0 + BK < K) ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, k0 + BK, t);
+    const bool more = k0 + BK < K;
+    if (more) ld.load(A, sam, sak, B, sbk, sbn, M, N, K, m0, n0, k0 + BK, t, vec_a, vec_b);
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       // rows ty*4 + {0..3} and 64 + ty*4 + {0..3}; columns tx*4 + {0..3} and 64 + tx*4 + {0..3}
       T a[8], b[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = As[kk][ty * 4 + i];
-        a[4 + i] = As[kk][64 + ty * 4 + i];
-        b[i] = Bs[kk][tx * 4 + i];
-        b[4 + i] = Bs[kk][64 + tx * 4 + i];
-      }
+      frag4(&As[cur][kk][ty * 4], a);
+      frag4(&As[cur][kk][64 + ty * 4], a + 4);
+      frag4(&Bs[cur][kk][tx * 4], b);
+      frag4(&Bs[cur][kk][64 + tx * 4], b + 4);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
     }
+    if (more) ld.store(As[cur ^ 1], Bs[cur ^ 1], a_kcontig, b_ncontig, t);  // the other buffer: read a step ago
+    __syncthreads();
+    cur ^= 1;
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -110,7 +152,11 @@ cudaError_t gemm(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, cons
                  const T* B, int64_t sbk, int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn) {
   if (M == 0 || N == 0) return cudaSuccess;
   dim3 grid(static_cast<unsigned>(ceil_div(N, BN)), static_cast<unsigned>(ceil_div(M, BM)));
-  gemm_kernel<T><<<grid, 256, 0, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn);
+  // A: unit stride along K (sak == 1) or along M (sam == 1); B: along N (sbn == 1) or along K
+  const bool vec_a = sak == 1 ? vec4_ok(A, sam, sak, K) : vec4_ok(A, sak, sam, M);
+  const bool vec_b = sbn == 1 ? vec4_ok(B, sbk, sbn, N) : vec4_ok(B, sbn, sbk, K);
+  gemm_kernel<T><<<grid, 256, 0, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn, vec_a,
+                                       vec_b);
   return cudaGetLastError();
 }
 

@@ -107,15 +107,18 @@ def test_two_gpu_vocab_parallel_matches_single_gpu(tmp_path):
                 assert rel_err(torch.from_numpy(z[f"{mode}_{k}"]), torch.from_numpy(z[f"g{k}"])) < 1e-6, (mode, k)
 
 
-@pytest.mark.parametrize("G", [2, 3, 8])
-def test_sharded_compute_on_one_gpu(G):
+@pytest.mark.parametrize("G,mode", [(2, "bf16"), (3, "bf16"), (8, "bf16"), (3, "fp32_params"), (2, "wide")])
+def test_sharded_compute_on_one_gpu(G, mode):
     """The vocabulary-sharded path's GPU work on one device: every shard's partial forward
-    (swvr_fwd_partial) and shard backward (dh partial in fp32, local dW / dE / db), merged as
-    the ranks merge them -- states stacked in rank order through swvr_combine, dh partials
-    summed -- with only the NCCL transport replaced by in-process stacking.  Checked against
-    the single-GPU API on the full vocabulary and against the fp64 oracle.  Runs on one GPU, so
-    it needs no second device; the collectives themselves are covered by the gloo CPU tests
-    and the 2-GPU NCCL test above."""
+    (swvr_fwd_partial) and shard backward (dh partial in fp32, local dW / dE / db, the last
+    chunk's dW rows deferred and computed on a bounded set of SMs), merged as the ranks merge
+    them -- states stacked in rank order through swvr_combine, dh partials summed -- with only
+    the NCCL transport replaced by in-process stacking.  Checked against the single-GPU API on
+    the full vocabulary and against the fp64 oracle.  Modes: bf16 shards; fp32 shard
+    parameters computed in bf16 (autocast over fp32 parameters: W and E cast one vocabulary
+    chunk at a time); D = 300 (wider than the tensor-core kernels take: the exact fp32 engine).
+    Runs on one GPU, so it needs no second device; the collectives themselves are covered by
+    the gloo CPU tests and the 2-GPU NCCL test above."""
     import swvr_b200 as swvr
     from oracle import swvr_oracle as orc
     from swvr_b200 import vocab_parallel as vp
@@ -123,25 +126,33 @@ def test_sharded_compute_on_one_gpu(G):
 
     h, W, E, b, t, w = (x.cuda() for x in _inputs())
     cdt = torch.bfloat16
+    if mode == "fp32_params":
+        W, E, b = W.float(), E.float(), b.float()
+    elif mode == "wide":
+        E = (0.02 * torch.randn(V, 300, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16).cuda()
+    Dm = E.shape[1]
     spans = [vp.shard_range(V, G, r) for r in range(G)]
     states = [vp.NativeBackend.partial(h, W[a:z], E[a:z], b[a:z], 1.0, 4096, cdt) for a, z in spans]
     O, lse = vp.NativeBackend.combine(*(torch.stack([s[i] for s in states]) for i in range(3)))
-    O_ref, lse_ref = swvr.softmax_readout(h, W, E, b, chunk_size=4096)
+    with torch.autocast("cuda", dtype=torch.bfloat16, enabled=mode == "fp32_params"):
+        O_ref, lse_ref = swvr.softmax_readout(h, W, E, b, chunk_size=4096)
     assert rel_err(O, O_ref) < 2e-2
     assert float((lse - lse_ref).abs().max()) < 1e-2
     Oo, lo = orc.softmax_readout_reference(npy(h), npy(W), npy(E), npy(b))
     assert rel_err(O, Oo) < 2e-2 and float(np.abs(npy(lse) - lo).max()) < 1e-2
 
     g = torch.Generator().manual_seed(9)
-    gO = (0.02 * torch.randn(N, D, generator=g)).cuda()
+    gO = (0.02 * torch.randn(N, Dm, generator=g)).cuda()
     glse = (0.01 * torch.randn(N, generator=g)).cuda()
     dh = torch.zeros(N, K, dtype=torch.float32, device="cuda")
     gW, gE, gb = [], [], []
     for a, z in spans:
         d, x, y, c, finish = vp.NativeBackend.backward(gO, glse, h, W[a:z], E[a:z], b[a:z], O, lse, 1.0, 4096, cdt,
                                                        True, True, True, True)
-        finish(16)  # the last chunk's dW rows on a bounded set of SMs
+        if finish is not None:
+            finish(16)  # the last chunk's dW rows on a bounded set of SMs
         assert d.dtype == torch.float32 and d.shape == (N, K)
+        assert x.dtype == W.dtype and y.dtype == E.dtype and c.dtype == b.dtype
         dh += d
         gW.append(x), gE.append(y), gb.append(c)
     gr = orc.readout_grads(npy(h), npy(W), npy(E), npy(b), npy(gO), npy(glse))
