@@ -1,9 +1,11 @@
 """Parity at BASELINE's full sizes, on exactly the workloads bench.py measures.
 
 c1 (N=16384 as h [8, 2048, 1024], V=152064, D=16, no bias), c2 (the headline: N=16384,
-K=2560, V=152064, D=64, bias, Bernoulli(0.9) per-token weight, z-loss 1e-4) and c3 (N=8192,
+K=2560, V=152064, D=64, bias, Bernoulli(0.9) per-token weight, z-loss 1e-4), c3 (N=8192,
 K=4096, V=128256, D=128, the raw ``softmax_readout`` with a torch MSE on top against
-``E[randint] + N(0, 0.01)``), built by bench.py's own ``make_inputs`` / ``make_step``.
+``E[randint] + N(0, 0.01)``) and c4 (N=131072 as h [32, 4096, 4096], V=152064, D=64, bias,
+under ``torch.utils.checkpoint``, on one GPU), built by bench.py's own ``make_inputs`` /
+``make_step``.
 
 Two checkers, each within the north star's bf16 tolerance (2e-2 norm-wise relative, the
 reference's test_cuda.py:33-35,54; LSE 1e-2 absolute):
@@ -53,7 +55,7 @@ def _run(api, c, leaves):
     return loss.detach(), O, lse, grads
 
 
-@pytest.mark.parametrize("config", ["c1", "c2", "c3"])
+@pytest.mark.parametrize("config", ["c1", "c2", "c3", "c4"])
 def test_full_size_matches_the_reference_library(config):
     ref = load_reference()
     if ref is None:
