@@ -284,6 +284,18 @@ static int bwd_aux_loads() {
   return s ? (std::atoi(s) != 0 ? 1 : 0) : 1;
 }
 
+// Unit order of the score kernel: groups of this many vocabulary tiles walk the token splits
+// (tc::bwd_unit), so on 74 pairs about four token splits of h and 20 W tiles stream at a
+// time.  At c2 (11 token splits per 60-tile chunk) the kernel ran 1.145-1.152 ms per chunk
+// against 1.166-1.168 with every split of a vocabulary tile in a row (1), A/B on one box;
+// 12 was as good as 20, and 64-wide K stages (6 of them) lost 19 %.  SWVR_BWD_GROUP
+// overrides it (read on each call).
+static int bwd_group(int VTc) {
+  const char* s = std::getenv("SWVR_BWD_GROUP");
+  const int v = s ? std::max(1, std::atoi(s)) : 20;
+  return std::max(1, std::min(v, std::max(VTc, 1)));
+}
+
 // Token splits of the score kernel's units (a 256-row vocabulary tile x a range of token
 // tiles): minimise the rounds over the pairs times the tiles per unit.
 static void choose_ts(int VTc, int NT, int sms, int* TS, int* per_t) {
@@ -441,6 +453,7 @@ static int tc_bwd(const swvr_problem& p, const swvr_grads& g, void* ws, size_t w
     sp.TS = TS;
     sp.per_t = per_t;
     sp.units = VTc * TS;
+    sp.gv = bwd_group(VTc);
     sp.ds = ds;
     sp.ld_ds = b.Npad;
     sp.part_de = part_de;

@@ -61,12 +61,26 @@ struct BwdScoresParams {
   const float* delta;  // [N]
   int NT, VT;          // BN-token tiles, 256-row vocabulary pair tiles of the chunk
   int TS, per_t, units;  // token splits, token tiles per split, VT * TS
+  int gv;              // unit order: groups of gv vocabulary tiles walk the token splits split-major
   void* ds;            // dS^T [chunk rows, ld_ds] in the compute dtype, or null (ld_ds >= NT*BN)
   int64_t ld_ds;
   float* part_de;      // [units * 256 * D] or null
   float* part_db;      // [units * 256] or null
   int aux_loads;       // 1: warp 2 loads gO and E, so the W / h stream never waits on their buffers
 };
+
+// Work unit u -> (256-row vocabulary tile vt, token split ts).  Consecutive units run at the
+// same time on consecutive pairs: groups of gv vocabulary tiles take the token splits one
+// after another, so about 74 / gv splits of h and gv W tiles stream together (gv = 1: every
+// split of a vocabulary tile in a row, so all of h streams in each round of units).  The
+// partial dE / db slot of a unit is vt * TS + ts whatever the order.
+__host__ __device__ inline void bwd_unit(const BwdScoresParams& p, int u, int* vt, int* ts) {
+  const int gsize = p.gv * p.TS;
+  const int grp = u / gsize, r = u % gsize;
+  const int rows = min(p.gv, p.VT - grp * p.gv);  // vocabulary tiles in this (possibly last, short) group
+  *ts = r / rows;
+  *vt = grp * p.gv + r % rows;
+}
 
 struct BwdScoresMaps {
   CUtensorMap w;    // W, box {64, 128}

@@ -183,7 +183,8 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t stage = 0, sphase = 0, g = 0, uc = 0;
       int prev_it = 0;  // token tile of the previous tile of this pair (double-buffered S)
       for (int u = pair; u < p.units; u += npairs) {
-        const int vt = u / p.TS, ts = u % p.TS;
+        int vt, ts;
+        bwd_unit(p, u, &vt, &ts);
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         if (it1 <= it0) continue;
         const int vrow0 = p.v_begin + vt * 256 + static_cast<int>(rank) * 128;
@@ -271,7 +272,8 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t g = 0, uc = 0;
       int prev_it = 0;
       for (int u = pair; u < p.units; u += npairs) {
-        const int vt = u / p.TS, ts = u % p.TS;
+        int vt, ts;
+        bwd_unit(p, u, &vt, &ts);
         const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
         if (it1 <= it0) continue;
         const int vrow0 = p.v_begin + vt * 256 + static_cast<int>(rank) * 128;
@@ -391,7 +393,8 @@ __global__ void __launch_bounds__(256, 1)
       if constexpr (Cfg::kSingleS) {
         // one S buffer: each tile's S, dP, gradient pass and dE before the next tile's S
         for (int u = pair; u < p.units; u += npairs) {
-          const int ts = u % p.TS;
+          int vt, ts;
+          bwd_unit(p, u, &vt, &ts);
           const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
           const int n = it1 - it0;
           if (n <= 0) continue;
@@ -419,7 +422,8 @@ __global__ void __launch_bounds__(256, 1)
         bool prev_first = false, prev_last = false;  // the previous tile opens / closes its unit
         uint32_t prev_uc = 0;                        // and its unit
         for (int u = pair; u < p.units; u += npairs) {
-          const int ts = u % p.TS;
+          int vt, ts;
+          bwd_unit(p, u, &vt, &ts);
           const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
           const int n = it1 - it0;
           if (n <= 0) continue;
@@ -496,7 +500,8 @@ __global__ void __launch_bounds__(256, 1)
     pdl_wait();
     uint32_t g = 0, uc = 0, q = 0;
     for (int u = pair; u < p.units; u += npairs) {
-      const int vt = u / p.TS, ts = u % p.TS;
+      int vt, ts;
+      bwd_unit(p, u, &vt, &ts);
       const int it0 = ts * p.per_t, it1 = min(it0 + p.per_t, p.NT);
       if (it1 <= it0) continue;
       const int local_row0 = vt * 256 + static_cast<int>(rank) * 128;  // within the chunk
@@ -572,7 +577,7 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
       }
-      const int64_t slot = static_cast<int64_t>(u) * 256 + static_cast<int>(rank) * 128 + r;
+      const int64_t slot = static_cast<int64_t>(vt * p.TS + ts) * 256 + static_cast<int>(rank) * 128 + r;
       if (need_de) {
         if (!warp_wait(de_full, uc & 1u, abort_flag, kErrBwdScores | 12)) goto done;
         tc_fence_after();

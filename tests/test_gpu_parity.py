@@ -539,6 +539,33 @@ def test_backward_token_tiles_agree(monkeypatch, N, K, V, D, chunk):
     assert rel_err(b[2], a[2]) < 1e-3 and rel_err(b[3], a[3]) < 1e-3
 
 
+@pytest.mark.parametrize("tile", ["128", "192"])
+def test_backward_unit_order_is_bit_exact(monkeypatch, tile):
+    """The score kernel's unit order (SWVR_BWD_GROUP: vocabulary tiles per group walking the
+    token splits) changes which pair computes which (vocabulary tile, token split) and when,
+    never what a unit computes or where its partial dE / db lands: every gradient is
+    bit-identical for groups of 1 (splits of a tile in a row), 3 and 7 (short last groups) and
+    one group for the whole chunk.  Checked against the oracle too."""
+    N, K, V, D = 3000, 1024, 12011, 64
+    monkeypatch.setenv("SWVR_BWD_TOKEN_TILE", tile)
+    inputs = make_gpu(N, K, V, D, torch.bfloat16, seed=17)
+    g = torch.Generator().manual_seed(14)
+    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
+    res = {}
+    for grp in ("1", "3", "7", "1000"):
+        monkeypatch.setenv("SWVR_BWD_GROUP", grp)
+        xs = [x.detach().clone().requires_grad_(True) for x in inputs]
+        O, lse = swvr.softmax_readout(*xs, chunk_size=4096)
+        torch.autograd.backward([O, lse], [gO, glse])
+        res[grp] = [x.grad for x in xs]
+    for grp in ("3", "7", "1000"):
+        for n, a, b in zip(["gh", "gW", "gE", "gb"], res["1"], res[grp]):
+            assert torch.equal(a, b), (grp, n)
+    _, _, gr = oracle_eager(*inputs, 1.0, gO, glse)
+    for n, a, r in zip(["gh", "gW", "gE", "gb"], res["7"], gr):
+        assert rel_err(a, r) < 2e-2, (n, rel_err(a, r))
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_reference_rise_inside_a_tile(dtype):
     """Scores that climb past the forward's emergency margin (64 octaves for bf16, 8 for fp16)
