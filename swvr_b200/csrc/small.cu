@@ -2,6 +2,7 @@
 // the deterministic dE / db reduction, the backward prologue, the MSE / z-loss epilogue
 // and dtype casts.
 #include <cmath>
+#include <type_traits>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -30,9 +31,10 @@ static cudaError_t launch_small(void (*kern)(KArgs...), unsigned blocks, unsigne
 // Source s of row n lives at idx(s, n): split slots of the tensor-core forward (mode 0,
 // T = tile_rows: ((n/T)*splits + s)*T + n%T) or shard-major arrays (mode 1: s*N + n).
 // One warp per row: the lanes split the sources for the max and the weights
-// w_s = 2^(m2_s - max) (exp2f for fp32 state), then split the D columns; the sums run in
-// double in source order for every column, and through a fixed shuffle tree for l, so the
-// result is deterministic and identical on every device that merges the same states.
+// w_s = 2^(m2_s - max) (exp2f for fp32 state), then split the D columns; the column sums
+// run in the state's precision as fused multiply-adds in source order, and l in double
+// through a fixed shuffle tree, so the result is deterministic and identical on every device
+// that merges the same states.
 __device__ __forceinline__ float exp2_t(float x) { return exp2f(x); }
 __device__ __forceinline__ double exp2_t(double x) { return exp2(x); }
 
@@ -65,15 +67,25 @@ __global__ void combine_kernel(int S, int64_t N, int64_t D, const T* __restrict_
   const double L = Lp;
   for (int64_t d0 = 0; d0 < D; d0 += 32) {  // uniform trip count: the shuffles below need every lane
     const int64_t d = d0 + lane;
-    double A = 0.0;
-    for (int s = 0; s < S; ++s) {
-      const T ws = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
-      const T w = s < 64 ? ws : exp2_t(m2[idx(s)] - ref);
-      if (d < D && w != T(0)) A += static_cast<double>(acc[idx(s) * D + d]) * static_cast<double>(w);
+    T A = 0;
+    // sources 8 at a time: their loads are all in flight before the first add; the adds stay
+    // in source order
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      T wv[8], v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int s = s0 + k;
+        const T ws = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
+        wv[k] = s < S ? (s < 64 ? ws : exp2_t(m2[idx(s)] - ref)) : T(0);
+        v[k] = (d < D && wv[k] != T(0)) ? acc[idx(s) * D + d] : T(0);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (d < D && wv[k] != T(0)) A = fma(v[k], wv[k], A);
     }
     if (d < D) {
-      if (O) O[n * D + d] = static_cast<T>(A / L);
-      if (acco) acco[n * D + d] = static_cast<T>(A);
+      if (O) O[n * D + d] = A / static_cast<T>(L);
+      if (acco) acco[n * D + d] = A;
     }
   }
   if (lane == 0) {
@@ -102,25 +114,45 @@ cudaError_t combine(int acc_dt, int S, int64_t N, int64_t D, const void* m2, con
 // ------------------------------------------------------------------ dE / db reduction
 // Row v of the chunk: sum its token-split partial slots in split order.  Slots are grouped
 // per vocabulary tile of `tile_rows` rows: slot((vt*TS + ts)*tile_rows + r), so for one
-// split the tile's rows x D floats are contiguous.  One thread per (row, column): the
-// loads of all splits are independent and go out together; the adds stay in split order.
+// split the tile's rows x D floats are contiguous.  One thread per (row, 4 columns) when D is
+// a multiple of 4 (else per (row, column)); each thread loads the splits 8 at a time, so
+// eight independent 16-byte loads are in flight before the first add, and the adds stay in
+// split order (the result does not depend on the batching).
+template <int VEC>
 __global__ void reduce_de_db_kernel(const float* __restrict__ part_de, const float* __restrict__ part_db, int TS,
                                     int n_ts, int v_begin, int rows, int tile_rows, int64_t D, void* gE, int gE_dt,
                                     int64_t ld_gE, void* gb, int gb_dt) {
+  using V = typename std::conditional<VEC == 4, float4, float>::type;
   pdl_wait();
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (part_de && i < static_cast<int64_t>(rows) * D) {
-    const int64_t total = static_cast<int64_t>(rows) * D;
-    const int rr = total < (int64_t(1) << 32) ? static_cast<int>(static_cast<uint32_t>(i) / static_cast<uint32_t>(D))
-                                              : static_cast<int>(i / D);
-    const int64_t d = i - static_cast<int64_t>(rr) * D;
+  const int64_t DV = D / VEC;  // vectors per row
+  if (part_de && i < static_cast<int64_t>(rows) * DV) {
+    const int64_t total = static_cast<int64_t>(rows) * DV;
+    const int rr = total < (int64_t(1) << 32) ? static_cast<int>(static_cast<uint32_t>(i) / static_cast<uint32_t>(DV))
+                                              : static_cast<int>(i / DV);
+    const int64_t d = (i - static_cast<int64_t>(rr) * DV) * VEC;
     const int vt = rr / tile_rows, r = rr % tile_rows;
-    const float* src = part_de + (static_cast<int64_t>(vt) * TS * tile_rows + r) * D + d;
-    const int64_t step = static_cast<int64_t>(tile_rows) * D;
-    float s = 0.f;
-#pragma unroll 4
-    for (int ts = 0; ts < n_ts; ++ts) s += src[ts * step];
-    store_f(gE, gE_dt, (v_begin + rr) * ld_gE + d, s);
+    const V* src = reinterpret_cast<const V*>(part_de + (static_cast<int64_t>(vt) * TS * tile_rows + r) * D + d);
+    const int64_t step = static_cast<int64_t>(tile_rows) * DV;  // one split, in vectors
+    float acc[VEC];
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) acc[c] = 0.f;
+    for (int ts0 = 0; ts0 < n_ts; ts0 += 8) {
+      V buf[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (ts0 + k < n_ts) buf[k] = src[(ts0 + k) * step];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (ts0 + k < n_ts) {
+          const float* f = reinterpret_cast<const float*>(&buf[k]);
+#pragma unroll
+          for (int c = 0; c < VEC; ++c) acc[c] += f[c];
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) store_f(gE, gE_dt, (v_begin + rr) * ld_gE + d + c, acc[c]);
   }
   if (part_db && i < rows) {
     const int rr = static_cast<int>(i);
@@ -138,9 +170,15 @@ cudaError_t reduce_de_db(const float* part_de, const float* part_db, int TS, int
                          cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const int n_ts = std::min(TS, static_cast<int>(ceil_div(NT, std::max(per_t, 1))));  // splits with tokens
-  const int64_t work = std::max<int64_t>(part_de ? static_cast<int64_t>(rows) * D : 0, rows);
-  return launch_small(reduce_de_db_kernel, static_cast<unsigned>(ceil_div(work, 256)), 256, pdl, st, part_de, part_db,
-                      TS, n_ts, v_begin, rows, tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
+  // 16-byte loads: D a multiple of 4 keeps every row (and the 256-byte aligned base) 16-byte aligned
+  const bool vec = D % 4 == 0 && (reinterpret_cast<uintptr_t>(part_de) & 15u) == 0;
+  const int64_t work = std::max<int64_t>(part_de ? static_cast<int64_t>(rows) * (vec ? D / 4 : D) : 0, rows);
+  const unsigned blocks = static_cast<unsigned>(ceil_div(work, 256));
+  if (vec)
+    return launch_small(reduce_de_db_kernel<4>, blocks, 256, pdl, st, part_de, part_db, TS, n_ts, v_begin, rows,
+                        tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
+  return launch_small(reduce_de_db_kernel<1>, blocks, 256, pdl, st, part_de, part_db, TS, n_ts, v_begin, rows,
+                      tile_rows, D, gE, gE_dt, ld_gE, gb, gb_dt);
 }
 
 // ------------------------------------------------------------------ bounded-wait self test
