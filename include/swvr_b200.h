@@ -201,6 +201,34 @@ int swvr_mse_bwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void*
                  void* grad_weight, void* stream);
 
 /*
+ * RMSNorm producer of h, fused at both ends of the readout (no counterpart in the reference,
+ * whose callers normalise the trunk's output before swvr.softmax_readout_mse; this is the
+ * "final norm feeding the readout" of its model code, kept inside the library).
+ *
+ * Forward: h[n, k] = x[n, k] * rstd[n] * weight[k] with rstd[n] = 1 / sqrt(mean_k x[n, k]^2 +
+ * eps), computed in fp32 (fp64 when x or h is F64) and rounded once into h's dtype (the
+ * readout's compute dtype, so the readout reads it as written).  weight may be NULL (1).
+ * rstd is fp32 [n_rows] (fp64 when x or h is F64).  x and h rows are ld_x / ld_h elements apart.
+ *
+ * Backward: grad_h is the readout's un-cast dh accumulator (swvr_grads.grad_h_acc: fp32, or
+ * fp64 for F64 compute) [n_rows, hidden], with rstd in the same dtype (acc_dtype).  Writes,
+ * where not NULL, grad_x [n_rows, hidden] (contiguous) and grad_weight [hidden]:
+ *   grad_x = rstd * (a - xh * mean_k(a * xh)),  a = grad_h * weight,  xh = x * rstd
+ *   grad_weight = sum_n grad_h * xh   (fixed-order reduction: deterministic)
+ * The workspace (swvr_rmsnorm_bwd_workspace_size) holds per-block partial weight gradients;
+ * SWVR_ERR_UNSUPPORTED when hidden is too wide for them (above 51200 fp32 columns).
+ */
+int swvr_rmsnorm_fwd(int64_t n_rows, int64_t hidden, const void* x, int32_t x_dtype, int64_t ld_x, const void* weight,
+                     int32_t weight_dtype, double eps, void* h, int32_t h_dtype, int64_t ld_h, void* rstd,
+                     void* stream);
+int swvr_rmsnorm_bwd_workspace_size(int64_t n_rows, int64_t hidden, int32_t acc_dtype, int32_t need_grad_weight,
+                                    size_t* bytes);
+int swvr_rmsnorm_bwd(int64_t n_rows, int64_t hidden, const void* grad_h, int32_t acc_dtype, const void* x,
+                     int32_t x_dtype, int64_t ld_x, const void* weight, int32_t weight_dtype, const void* rstd,
+                     void* grad_x, int32_t grad_x_dtype, void* grad_weight, int32_t grad_weight_dtype, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/*
  * Launch accounting for benchmarks (no counterpart in the reference).  Between
  * swvr_profile_start() and swvr_profile_stop(), every kernel the library launches from any
  * host thread is counted per kind and bracketed by a pair of CUDA events on its stream.

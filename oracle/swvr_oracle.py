@@ -14,6 +14,9 @@ It restates, in numpy, the algorithm of the reference library pengzhangzhi/swvr:
 * ``readout_grads``              -- analytic gradients of the eager oracle (the autograd of
                                     swvr/reference.py:5-14, written out).
 * ``mse_forward`` / ``mse_backward`` -- the loss epilogue of swvr/api.py:44-66 and its gradient.
+* ``rmsnorm_forward`` / ``rmsnorm_backward`` -- the RMSNorm that the fused producer of h
+                                    computes (torch.nn.functional.rms_norm over the last
+                                    dimension; not part of the reference), in fp64.
 
 Precision is restated exactly as the reference's torch path has it (swvr/chunked.py:1-13):
 matrix-product operands are rounded to the compute dtype ``cdt`` (bf16/fp16 emulated by
@@ -307,3 +310,34 @@ def shard_partials(h, W, E, bias, logit_scale, G):
         ls.append(p.sum(1))
         accs.append(p @ np.asarray(E[v0:v1], np.float64))
     return np.stack(m2s), np.stack(ls), np.stack(accs)
+
+
+# ---------------------------------------------------------------------------------------------
+# RMSNorm producer of h (no counterpart in the reference; the norm of
+# torch.nn.functional.rms_norm over the last dimension, fp64)
+# ---------------------------------------------------------------------------------------------
+
+
+def rmsnorm_forward(x, weight=None, eps=1e-6):
+    """(h, rstd): h = x * rstd * weight, rstd = 1 / sqrt(mean_k x^2 + eps), in fp64."""
+    x = np.asarray(x, dtype=np.float64)
+    rstd = 1.0 / np.sqrt((x * x).mean(axis=-1) + eps)
+    h = x * rstd[..., None]
+    if weight is not None:
+        h = h * np.asarray(weight, dtype=np.float64)
+    return h, rstd
+
+
+def rmsnorm_backward(dh, x, weight=None, eps=1e-6):
+    """(dx, dweight) of rmsnorm_forward for the upstream gradient dh, in fp64:
+    dx = rstd * (a - xh * mean_k(a * xh)) with a = dh * weight and xh = x * rstd;
+    dweight = sum over rows of dh * xh (None without a weight)."""
+    x = np.asarray(x, dtype=np.float64)
+    dh = np.asarray(dh, dtype=np.float64)
+    _, rstd = rmsnorm_forward(x, None, eps)
+    xh = x * rstd[..., None]
+    g = np.ones(x.shape[-1]) if weight is None else np.asarray(weight, dtype=np.float64)
+    a = dh * g
+    dx = rstd[..., None] * (a - xh * (a * xh).mean(axis=-1, keepdims=True))
+    dw = None if weight is None else (dh * xh).reshape(-1, x.shape[-1]).sum(axis=0)
+    return dx, dw

@@ -74,6 +74,11 @@ _SIGNATURES = {
     "swvr_mse_bwd": (c_int, [c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_double,
                              c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "swvr_fwd_noalloc": (c_int, [POINTER(Problem), c_void_p, c_void_p, c_void_p]),
+    "swvr_rmsnorm_fwd": (c_int, [c_int64, c_int64, c_void_p, c_int32, c_int64, c_void_p, c_int32, c_double, c_void_p,
+                                 c_int32, c_int64, c_void_p, c_void_p]),
+    "swvr_rmsnorm_bwd_workspace_size": (c_int, [c_int64, c_int64, c_int32, c_int32, POINTER(c_size_t)]),
+    "swvr_rmsnorm_bwd": (c_int, [c_int64, c_int64, c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p, c_int32,
+                                 c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_size_t, c_void_p]),
     "swvr_profile_start": (c_int, []),
     "swvr_profile_stop": (c_int, [POINTER(ProfileRecord), c_int, POINTER(c_int)]),
 }

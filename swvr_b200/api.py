@@ -80,19 +80,29 @@ class SoftmaxReadoutMSE(nn.Module):
     ``head`` may be an ``nn.Linear(K, V)`` (whose bias, if any, becomes the score bias) or a
     plain ``[V, K]`` weight; ``embedding`` an ``nn.Embedding(V, D)`` or a ``[V, D]`` table.
     The module stores the objects it is given, never copies, so tied weights and the
-    optimizer's view of the parameters are unaffected.
+    optimizer's view of the parameters are unaffected.  Optionally (not in the reference),
+    ``norm``, an ``nn.RMSNorm(K)``, is applied to the input first, fused into the library
+    (``rmsnorm_softmax_readout_mse``): ``forward`` then takes the trunk output before the norm.
     """
 
     def __init__(self, head, embedding, *, z_loss_weight=0.0, logit_scale=1.0,
-                 reduction="mean", chunk_size=None):
+                 reduction="mean", chunk_size=None, norm=None):
         super().__init__()
         self.head, self.embedding = head, embedding
         self.z_loss_weight, self.logit_scale = z_loss_weight, logit_scale
         self.reduction, self.chunk_size = reduction, chunk_size
+        if norm is not None:
+            from .norm import norm_parts
+            norm_parts(norm)  # validates it
+        self.norm = norm
 
     def forward(self, h, target, weight=None):
         bias = getattr(self.head, "bias", None) if isinstance(self.head, nn.Module) else None
-        return softmax_readout_mse(
-            h, _weight_of(self.head), _weight_of(self.embedding), target, bias,
-            weight=weight, reduction=self.reduction, z_loss_weight=self.z_loss_weight,
-            logit_scale=self.logit_scale, chunk_size=self.chunk_size)
+        kw = dict(weight=weight, reduction=self.reduction, z_loss_weight=self.z_loss_weight,
+                  logit_scale=self.logit_scale, chunk_size=self.chunk_size)
+        if self.norm is not None:
+            from .norm import norm_parts, rmsnorm_softmax_readout_mse
+            g, eps = norm_parts(self.norm)
+            return rmsnorm_softmax_readout_mse(h, g, _weight_of(self.head), _weight_of(self.embedding), target,
+                                               bias, eps=eps, **kw)
+        return softmax_readout_mse(h, _weight_of(self.head), _weight_of(self.embedding), target, bias, **kw)

@@ -52,10 +52,11 @@ static int num_sms() {
 
 // ---------------------------------------------------------------------------- launch accounting
 enum ProfKind { kProfFwd = 0, kProfBwdScores, kProfGemm, kProfCombine, kProfReduce, kProfPrologue, kProfCast,
-                kProfMse, kProfSimt, kProfKinds };
+                kProfMse, kProfSimt, kProfNorm, kProfKinds };
 static const char* kProfNames[kProfKinds] = {"fwd_kernel",      "bwd_scores_kernel", "gemm_kernel",
                                              "combine_kernel",  "reduce_de_db_kernel", "prologue_kernel",
-                                             "cast_kernel",     "mse_kernel",        "simt_kernels"};
+                                             "cast_kernel",     "mse_kernel",        "simt_kernels",
+                                             "rmsnorm_kernels"};
 static std::mutex g_prof_mu;
 static bool g_prof_on = false;
 static int64_t g_prof_launches[kProfKinds];
@@ -718,6 +719,69 @@ int swvr_mse_bwd(int64_t n_tokens, int64_t embed_dim, int32_t dtype, const void*
   ProfScope ps(kProfMse, static_cast<cudaStream_t>(stream));
   SWVR_CUDA(small::mse_bwd(dtype, n_tokens, embed_dim, O, lse, target, weight, z, reduction, grad_out, stats, grad_O,
                            grad_lse, grad_target, grad_weight, static_cast<cudaStream_t>(stream)));
+  return SWVR_OK;
+}
+
+
+// ------------------------------------------------------------------ RMSNorm producer of h
+static bool norm_dtype_ok(int32_t dt) { return dt == SWVR_F32 || dt == SWVR_F64 || dt == SWVR_BF16 || dt == SWVR_F16; }
+
+int swvr_rmsnorm_fwd(int64_t n_rows, int64_t hidden, const void* x, int32_t x_dtype, int64_t ld_x, const void* weight,
+                     int32_t weight_dtype, double eps, void* h, int32_t h_dtype, int64_t ld_h, void* rstd,
+                     void* stream) {
+  if (n_rows < 0 || hidden <= 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "n_rows must be >= 0 and hidden > 0");
+  if (!norm_dtype_ok(x_dtype) || !norm_dtype_ok(h_dtype) || (weight && !norm_dtype_ok(weight_dtype)))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (ld_x < hidden || ld_h < hidden) return fail(SWVR_ERR_INVALID_ARGUMENT, "row pitch below hidden");
+  if (!(eps >= 0.0)) return fail(SWVR_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+  if (n_rows > 0 && (!x || !h || !rstd)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ProfScope ps(kProfNorm, st);
+  if (x_dtype == SWVR_F64 || h_dtype == SWVR_F64)
+    SWVR_CUDA(norm::fwd<double>(n_rows, hidden, x, x_dtype, ld_x, weight, weight_dtype, eps, h, h_dtype, ld_h, rstd, st));
+  else
+    SWVR_CUDA(norm::fwd<float>(n_rows, hidden, x, x_dtype, ld_x, weight, weight_dtype, eps, h, h_dtype, ld_h, rstd, st));
+  return SWVR_OK;
+}
+
+int swvr_rmsnorm_bwd_workspace_size(int64_t n_rows, int64_t hidden, int32_t acc_dtype, int32_t need_grad_weight,
+                                    size_t* bytes) {
+  if (!bytes) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (n_rows < 0 || hidden <= 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "n_rows must be >= 0 and hidden > 0");
+  if (acc_dtype != SWVR_F32 && acc_dtype != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "acc dtype must be F32/F64");
+  *bytes = norm::bwd_workspace(n_rows, hidden, dtype_size(acc_dtype), need_grad_weight != 0);
+  return SWVR_OK;
+}
+
+int swvr_rmsnorm_bwd(int64_t n_rows, int64_t hidden, const void* grad_h, int32_t acc_dtype, const void* x,
+                     int32_t x_dtype, int64_t ld_x, const void* weight, int32_t weight_dtype, const void* rstd,
+                     void* grad_x, int32_t grad_x_dtype, void* grad_weight, int32_t grad_weight_dtype, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (n_rows < 0 || hidden <= 0) return fail(SWVR_ERR_INVALID_ARGUMENT, "n_rows must be >= 0 and hidden > 0");
+  if (acc_dtype != SWVR_F32 && acc_dtype != SWVR_F64) return fail(SWVR_ERR_INVALID_ARGUMENT, "acc dtype must be F32/F64");
+  if (!norm_dtype_ok(x_dtype) || (weight && !norm_dtype_ok(weight_dtype)) ||
+      (grad_x && !norm_dtype_ok(grad_x_dtype)) || (grad_weight && !norm_dtype_ok(grad_weight_dtype)))
+    return fail(SWVR_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (ld_x < hidden) return fail(SWVR_ERR_INVALID_ARGUMENT, "row pitch below hidden");
+  if (grad_weight && !weight) return fail(SWVR_ERR_INVALID_ARGUMENT, "grad_weight without weight");
+  if (!grad_x && !grad_weight) return SWVR_OK;
+  if (n_rows > 0 && (!grad_h || !x || !rstd)) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL pointer");
+  const size_t asz = dtype_size(acc_dtype);
+  const bool need_w = grad_weight != nullptr;
+  if (need_w && norm::bwd_shape(n_rows, hidden, asz, true).nwarps < 1)
+    return fail(SWVR_ERR_UNSUPPORTED, "hidden %lld too wide for the weight-gradient sums in shared memory",
+                static_cast<long long>(hidden));
+  const size_t need = norm::bwd_workspace(n_rows, hidden, asz, need_w);
+  if (workspace_bytes < need) return fail(SWVR_ERR_WORKSPACE, "workspace %zu < required %zu", workspace_bytes, need);
+  if (need && !workspace) return fail(SWVR_ERR_INVALID_ARGUMENT, "NULL workspace");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ProfScope ps(kProfNorm, st);
+  if (acc_dtype == SWVR_F64)
+    SWVR_CUDA(norm::bwd<double>(n_rows, hidden, grad_h, x, x_dtype, ld_x, weight, weight_dtype, rstd, grad_x,
+                                grad_x_dtype, grad_weight, grad_weight_dtype, workspace, st));
+  else
+    SWVR_CUDA(norm::bwd<float>(n_rows, hidden, grad_h, x, x_dtype, ld_x, weight, weight_dtype, rstd, grad_x,
+                               grad_x_dtype, grad_weight, grad_weight_dtype, workspace, st));
   return SWVR_OK;
 }
 

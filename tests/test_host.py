@@ -134,7 +134,8 @@ def test_module_holds_references():
     assert m.head is head and m.embedding is emb
     assert swvr.__version__ == "0.1.0"
     assert set(swvr.__all__) == {"softmax_readout", "softmax_readout_mse", "SoftmaxReadoutMSE",
-                                 "softmax_readout_reference"}
+                                 "softmax_readout_reference", "rmsnorm_softmax_readout",
+                                 "rmsnorm_softmax_readout_mse"}
 
 
 def test_wide_embedding_and_chunk_planning():
