@@ -430,10 +430,14 @@ def run_ours(args, c, rank, world, device):
     e2e_run(2)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    e2e_run(args.steps)
-    e1.record(stream)
-    barrier()
+    with ClockSampler(device) as e2e_clocks:
+        barrier()
+        e2e_clocks.mark_start()
+        e0.record(stream)
+        e2e_run(args.steps)
+        e1.record(stream)
+        barrier()
+        e2e_clocks.mark_end()
     ms_e2e = e0.elapsed_time(e1) / args.steps
 
     # max over ranks
@@ -441,7 +445,8 @@ def run_ours(args, c, rank, world, device):
     if world > 1:
         dist.all_reduce(t_local, op=dist.ReduceOp.MAX)
     ms, ms_e2e = t_local.tolist()
-    return dict(ms=ms, ms_e2e=ms_e2e, prof=prof.result, clocks=clocks.summary(), peak_gib=peak_gib, h2d=h2d,
+    return dict(ms=ms, ms_e2e=ms_e2e, prof=prof.result, clocks=clocks.summary(), e2e_clocks=e2e_clocks.summary(),
+                peak_gib=peak_gib, h2d=h2d,
                 loss=float(loss_host), Vr=Vr, checksums=sums)
 
 
@@ -729,7 +734,8 @@ def main():
                                   "host memory and NVLink all-gathers the rest (vocab_parallel.replicate_from_host)"
                                   if world > 1 else "whole job: pinned host buffers, double-buffered on the device; step "
                                   "i+1's inputs are copied on a side stream while step i computes, every copy inside "
-                                  "the timed region")},
+                                  "the timed region"),
+                    "clocks": r["e2e_clocks"]},
         }
         if ref_gpu is not None:
             if "unavailable" not in ref_gpu:
