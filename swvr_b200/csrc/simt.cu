@@ -1,7 +1,11 @@
-// Exact SIMT CUDA path for fp32 / fp64 compute: the chunked algorithm of the reference
+// Exact path for fp32 / fp64 compute: the chunked algorithm of the reference
 // (swvr/chunked.py:82-151, torch branch) with every GEMM and element-wise step as a CUDA
 // kernel.  Used for SWVR_F32 / SWVR_F64 compute dtypes (gradcheck, fp32 parity), where the
-// tensor cores' bf16/fp16 operands would not meet the fp32 1e-5 / fp64 tolerances.
+// bf16/fp16 tensor-core kernels would not meet the fp32 1e-5 / fp64 tolerances.  fp64 GEMMs
+// run on the CUDA cores; fp32 GEMMs run as three-term split TF32 products on the tensor
+// cores (gemm_tf32x3_kernel, fp32-level error) wherever their operands can be staged 16
+// bytes at a time, and on the CUDA cores otherwise.
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -147,6 +151,245 @@ __global__ void __launch_bounds__(256) gemm_kernel(int64_t M, int64_t N, int64_t
   }
 }
 
+// fp32 GEMM on the tensor cores at fp32 accuracy: each operand is split into a TF32 head and
+// the TF32 rounding of its remainder, x = hi(x) + lo(x), and the product takes the three
+// terms lo·hi + hi·lo + hi·hi in fp32 accumulation (the lo·lo term, ~2^-22 relative, is
+// dropped): about 2^-21 relative error per product, against 2^-24 for an fp32 FMA and 2^-11
+// for plain TF32.  128 x 128 block tiles, 32-deep K tiles in a 3-stage cp.async ring (the
+// CUDA-core kernel above, one 8-deep step ahead, waits on its global loads), eight warps of
+// 64 x 32 as 4 x 4 warp-level m16n8k8 TF32 MMAs; the operands are split as the fragments
+// are read.  Each operand is staged in its own global layout: a K-contiguous tile as rows of
+// 32 + 4 floats, an M- (or N-) contiguous one as rows of 128 + 8; in both a fragment load of
+// lane (g = lane / 4, q = lane % 4) touches 32 distinct banks.
+namespace tf32x3 {
+constexpr int TM = 128, TN = 128, TK = 32, STAGES = 3, KP = TK + 4, MP = 128 + 8;
+constexpr int A_WORDS = TM * KP > TK * MP ? TM * KP : TK * MP;  // either layout of one stage
+constexpr int B_WORDS = TN * KP > TK * MP ? TN * KP : TK * MP;
+constexpr int SMEM = STAGES * (A_WORDS + B_WORDS) * 4;
+}  // namespace tf32x3
+
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// 16 bytes global -> shared, zero-filled when !in (no bytes are read then).
+__device__ __forceinline__ void cp16(float* dst, const float* src, bool in) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(in ? 16 : 0));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+// AK: A is K-contiguous (sak == 1) else M-contiguous (sam == 1); BNC: B is N-contiguous
+// (sbn == 1) else K-contiguous (sbk == 1).  The host checks the 16-byte alignment of every
+// staged chunk (see gemm below).
+template <bool AK, bool BNC>
+__global__ void __launch_bounds__(256, 2) gemm_tf32x3_kernel(int64_t M, int64_t N, int64_t K, float alpha,
+                                                          const float* __restrict__ A, int64_t sam, int64_t sak,
+                                                          const float* __restrict__ B, int64_t sbk, int64_t sbn,
+                                                          float beta, void* C, int cdt, int64_t scm, int64_t scn,
+                                                          int64_t kper, int64_t zstride, const void* cbias,
+                                                          int cbias_dt) {
+  using namespace tf32x3;
+  // split K: block z takes K rows [z * kper, z * kper + kper) and writes its own fp32 slice of C
+  {
+    const int64_t kb = static_cast<int64_t>(blockIdx.z) * kper;
+    A += kb * sak;
+    B += kb * sbk;
+    K = K - kb < kper ? K - kb : kper;
+    if (gridDim.z > 1) C = static_cast<float*>(C) + blockIdx.z * zstride;
+  }
+  extern __shared__ __align__(16) float smem_f[];
+  float* As = smem_f;                       // [STAGES][A_WORDS]
+  float* Bs = smem_f + STAGES * A_WORDS;    // [STAGES][B_WORDS]
+  const int t = threadIdx.x, lane = t % 32, warp = t / 32;
+  const int g = lane / 4, q = lane % 4;
+  const int wm = (warp % 2) * 64, wn = (warp / 2) * 32;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * TM, n0 = static_cast<int64_t>(blockIdx.x) * TN;
+  const int ktiles = static_cast<int>((K + TK - 1) / TK);
+
+  // stage s <- K tile kt: 1024 16-byte chunks of A and of B, 4 + 4 per thread
+  auto load = [&](int s, int kt) {
+    const int64_t k0 = static_cast<int64_t>(kt) * TK;
+    float* as = As + s * A_WORDS;
+    float* bs = Bs + s * B_WORDS;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = t + i * 256;
+      if (AK) {  // 128 rows of m x 8 chunks of k
+        const int r = c / 8, c4 = (c % 8) * 4;
+        const int64_t m = m0 + r, k = k0 + c4;
+        const bool in = m < M && k < K;
+        cp16(as + r * KP + c4, in ? A + m * sam + k : A, in);
+      } else {   // 32 rows of k x 32 chunks of m
+        const int r = c / 32, c4 = (c % 32) * 4;
+        const int64_t k = k0 + r, m = m0 + c4;
+        const bool in = m < M && k < K;
+        cp16(as + r * MP + c4, in ? A + k * sak + m : A, in);
+      }
+      if (BNC) { // 32 rows of k x 32 chunks of n
+        const int r = c / 32, c4 = (c % 32) * 4;
+        const int64_t k = k0 + r, n = n0 + c4;
+        const bool in = n < N && k < K;
+        cp16(bs + r * MP + c4, in ? B + k * sbk + n : B, in);
+      } else {   // 128 rows of n x 8 chunks of k
+        const int r = c / 8, c4 = (c % 8) * 4;
+        const int64_t n = n0 + r, k = k0 + c4;
+        const bool in = n < N && k < K;
+        cp16(bs + r * KP + c4, in ? B + n * sbn + k : B, in);
+      }
+    }
+  };
+  auto a_at = [&](const float* as, int r, int k) -> float { return AK ? as[r * KP + k] : as[k * MP + r]; };
+  auto b_at = [&](const float* bs, int k, int n) -> float { return BNC ? bs[k * MP + n] : bs[n * KP + k]; };
+
+  float acc[4][4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < ktiles) load(s, s);
+    cp_commit();
+  }
+  for (int kt = 0; kt < ktiles; ++kt) {
+    cp_wait<STAGES - 2>();  // K tile kt has landed (this thread's copies) ...
+    __syncthreads();        // ... and every thread's; the stage read in kt - 1 is free again
+    if (kt + STAGES - 1 < ktiles) load((kt + STAGES - 1) % STAGES, kt + STAGES - 1);
+    cp_commit();
+    const float* as = As + (kt % STAGES) * A_WORDS;
+    const float* bs = Bs + (kt % STAGES) * B_WORDS;
+#pragma unroll
+    for (int kk = 0; kk < TK; kk += 8) {
+      uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        split_tf32(b_at(bs, kk + q, wn + j * 8 + g), bh[j][0], bl[j][0]);
+        split_tf32(b_at(bs, kk + q + 4, wn + j * 8 + g), bh[j][1], bl[j][1]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = wm + i * 16 + g;
+        uint32_t ah[4], al[4];
+        split_tf32(a_at(as, r, kk + q), ah[0], al[0]);
+        split_tf32(a_at(as, r + 8, kk + q), ah[1], al[1]);
+        split_tf32(a_at(as, r, kk + q + 4), ah[2], al[2]);
+        split_tf32(a_at(as, r + 8, kk + q + 4), ah[3], al[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          mma_tf32(acc[i][j], al, bh[j]);  // small terms first
+          mma_tf32(acc[i][j], ah, bl[j]);
+          mma_tf32(acc[i][j], ah, bh[j]);
+        }
+      }
+    }
+  }
+  cp_wait<0>();
+  // accumulator fragment e of tile (i, j): row g (+8 for e >= 2), column 2q (+1 for odd e)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {
+      const int64_t gm = m0 + wm + i * 16 + g + e2 * 8;
+      if (gm >= M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e1 = 0; e1 < 2; ++e1) {
+          const int64_t gn = n0 + wn + j * 8 + 2 * q + e1;
+          if (gn >= N) continue;
+          const int64_t off = gm * scm + gn * scn;
+          float v = alpha * acc[i][j][e2 * 2 + e1];
+          if (beta != 0.f) v += beta * load_f(C, cdt, off);
+          if (cbias) v += load_f(cbias, cbias_dt, gn);  // the score bias of column gn (the S GEMM)
+          store_f(C, cdt, off, v);
+        }
+      }
+    }
+  }
+}
+
+// 16-byte staging needs: unit stride along the staged rows, a 16-byte aligned base, a row
+// pitch that is a multiple of 4 floats and an extent along the rows that is a multiple of 4
+// (a chunk is wholly inside or outside).
+static bool tf32x3_ok(const float* A, int64_t sam, int64_t sak, int64_t M, const float* B, int64_t sbk, int64_t sbn,
+                      int64_t N, int64_t K) {
+  const bool a_ok = sak == 1 ? vec4_ok(A, sam, sak, K) : (sam == 1 && vec4_ok(A, sak, sam, M));
+  const bool b_ok = sbn == 1 ? vec4_ok(B, sbk, sbn, N) : (sbk == 1 && vec4_ok(B, sbn, sbk, K));
+  return a_ok && b_ok;
+}
+
+template <bool AK, bool BNC>
+static cudaError_t launch_tf32x3(cudaStream_t st, dim3 grid, int64_t M, int64_t N, int64_t K, float alpha,
+                                 const float* A, int64_t sam, int64_t sak, const float* B, int64_t sbk, int64_t sbn,
+                                 float beta, void* C, int cdt, int64_t scm, int64_t scn, int64_t kper,
+                                 int64_t zstride, const void* cbias, int cbias_dt) {
+  auto kern = gemm_tf32x3_kernel<AK, BNC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tf32x3::SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 256, tf32x3::SMEM, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn, kper,
+                                        zstride, cbias, cbias_dt);
+  return cudaGetLastError();
+}
+
+static cudaError_t launch_tf32x3_any(cudaStream_t st, dim3 grid, int64_t M, int64_t N, int64_t K, float alpha,
+                                     const float* A, int64_t sam, int64_t sak, const float* B, int64_t sbk,
+                                     int64_t sbn, float beta, void* C, int cdt, int64_t scm, int64_t scn,
+                                     int64_t kper, int64_t zstride, const void* cbias = nullptr,
+                                     int cbias_dt = SWVR_F32) {
+  if (sak == 1)
+    return sbn == 1 ? launch_tf32x3<true, true>(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm,
+                                                 scn, kper, zstride, cbias, cbias_dt)
+                    : launch_tf32x3<true, false>(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt,
+                                                  scm, scn, kper, zstride, cbias, cbias_dt);
+  return sbn == 1 ? launch_tf32x3<false, true>(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm,
+                                                scn, kper, zstride, cbias, cbias_dt)
+                  : launch_tf32x3<false, false>(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt,
+                                                 scm, scn, kper, zstride, cbias, cbias_dt);
+}
+
+// C = alpha * sum_z part[z] + beta * C, the K splits summed in z order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M, int64_t N, float alpha,
+                                     float beta, void* C, int cdt, int64_t scm, int64_t scn) {
+  const int64_t MN = M * N;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < MN;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float t = 0.f;
+    for (int z = 0; z < splits; ++z) t += part[z * MN + i];
+    const int64_t off = (i / N) * scm + (i % N) * scn;
+    float v = alpha * t;
+    if (beta != 0.f) v += beta * load_f(C, cdt, off);
+    store_f(C, cdt, off, v);
+  }
+}
+
+// Floats of split-K partials the fp32 kernels may use for a GEMM whose output is M x N.
+constexpr int64_t kSplitKMaxFloats = int64_t(16) << 20;  // 64 MB
+inline int64_t splitk_floats(int64_t M, int64_t N) {
+  const int64_t want = 16 * M * N;
+  return want < kSplitKMaxFloats ? want : kSplitKMaxFloats;
+}
+
 template <typename T>
 cudaError_t gemm(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, const T* A, int64_t sam, int64_t sak,
                  const T* B, int64_t sbk, int64_t sbn, T beta, void* C, int cdt, int64_t scm, int64_t scn) {
@@ -155,9 +398,46 @@ cudaError_t gemm(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, cons
   // A: unit stride along K (sak == 1) or along M (sam == 1); B: along N (sbn == 1) or along K
   const bool vec_a = sak == 1 ? vec4_ok(A, sam, sak, K) : vec4_ok(A, sak, sam, M);
   const bool vec_b = sbn == 1 ? vec4_ok(B, sbk, sbn, N) : vec4_ok(B, sbn, sbk, K);
-  gemm_kernel<T><<<grid, 256, 0, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn, vec_a,
-                                       vec_b);
+  if constexpr (sizeof(T) == 4) {
+    // the tensor-core kernel where its 16-byte staging applies, else the CUDA-core one
+    if (tf32x3_ok(A, sam, sak, M, B, sbk, sbn, N, K))
+      return launch_tf32x3_any(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn, K, 0);
+  }
+  gemm_kernel<T><<<grid, 256, 0, st>>>(M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn, vec_a, vec_b);
   return cudaGetLastError();
+}
+
+// A GEMM whose output is narrow (the P.E and dE products, D columns) and whose K is long: its
+// 128 x 128 tiles would leave most SMs idle, so the fp32 kernel splits K into up to 16
+// ranges, about four 128 x 128 tiles per SM in all, each range writing an fp32 slice of
+// `part` (splitk_floats(M, N) floats), summed in order by splitk_reduce_kernel.  (Splitting
+// the dh and dW GEMMs as well, whose tiles already fill 86 % of two block slots per SM, made
+// the fp32 step 1.5 ms slower.)  fp64, or a layout the tensor-core kernel does not stage,
+// takes gemm().
+template <typename T>
+cudaError_t gemm_split(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, const T* A, int64_t sam,
+                        int64_t sak, const T* B, int64_t sbk, int64_t sbn, T beta, void* C, int cdt, int64_t scm,
+                        int64_t scn, float* part) {
+  if constexpr (sizeof(T) == 4) {
+    if (M > 0 && N > 0 && part && tf32x3_ok(A, sam, sak, M, B, sbk, sbn, N, K)) {
+      const int64_t tiles = ceil_div(M, tf32x3::TM) * ceil_div(N, tf32x3::TN);
+      int64_t splits = std::min<int64_t>({int64_t(16), ceil_div(4 * kNumSMsB200, tiles), K / 256,
+                                          splitk_floats(M, N) / (M * N)});
+      if (splits >= 2) {
+        const int64_t kper = round_up(ceil_div(K, splits), tf32x3::TK);
+        splits = ceil_div(K, kper);
+        dim3 grid(static_cast<unsigned>(ceil_div(N, tf32x3::TN)), static_cast<unsigned>(ceil_div(M, tf32x3::TM)),
+                  static_cast<unsigned>(splits));
+        cudaError_t e = launch_tf32x3_any(st, grid, M, N, K, 1.f, A, sam, sak, B, sbk, sbn, 0.f, part, SWVR_F32, N, 1,
+                                          kper, M * N);
+        if (e != cudaSuccess) return e;
+        splitk_reduce_kernel<<<static_cast<unsigned>(std::min<int64_t>(ceil_div(M * N, 256), 8 * kNumSMsB200)), 256, 0,
+                               st>>>(part, static_cast<int>(splits), M, N, alpha, beta, C, cdt, scm, scn);
+        return cudaGetLastError();
+      }
+    }
+  }
+  return gemm<T>(st, M, N, K, alpha, A, sam, sak, B, sbk, sbn, beta, C, cdt, scm, scn);
 }
 
 template <typename T>
@@ -197,6 +477,32 @@ __global__ void add_bias_kernel(T* S, int64_t N, int64_t C, const void* bias, in
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     S[i] += static_cast<T>(load_d(bias, bdt, v0 + i % C));
+}
+
+inline unsigned grid_for(int64_t n, int threads = 256) {
+  int64_t g = ceil_div(n, threads);
+  if (g < 1) g = 1;
+  if (g > 4096) g = 4096;
+  return static_cast<unsigned>(g);
+}
+
+// S[N, C] = alpha * A B + bias[v0 : v0 + C] (the bias of the chunk's scores, chunked.py:77-78):
+// added in the fp32 tensor-core GEMM's epilogue where that kernel runs, else by add_bias_kernel.
+template <typename T>
+static cudaError_t gemm_bias(cudaStream_t st, int64_t M, int64_t N, int64_t K, T alpha, const T* A, int64_t sam,
+                             int64_t sak, const T* B, int64_t sbk, int64_t sbn, T* S, int adt, const void* bias,
+                             int bdt, int64_t v0) {
+  if constexpr (sizeof(T) == 4) {
+    if (bias && M > 0 && N > 0 && tf32x3_ok(A, sam, sak, M, B, sbk, sbn, N, K)) {
+      dim3 grid(static_cast<unsigned>(ceil_div(N, BN)), static_cast<unsigned>(ceil_div(M, BM)));
+      return launch_tf32x3_any(st, grid, M, N, K, alpha, A, sam, sak, B, sbk, sbn, 0.f, S, adt, N, 1, K, 0,
+                               static_cast<const char*>(bias) + v0 * static_cast<int64_t>(dtype_size(bdt)), bdt);
+    }
+  }
+  cudaError_t e = gemm<T>(st, M, N, K, alpha, A, sam, sak, B, sbk, sbn, T(0), S, adt, N, 1);
+  if (e != cudaSuccess || !bias) return e;
+  add_bias_kernel<T><<<grid_for(M * N), 256, 0, st>>>(S, M, N, bias, bdt, v0);
+  return cudaGetLastError();
 }
 
 // One block per row: the online-softmax update of chunked.py:96-104 (P written over S).
@@ -276,14 +582,27 @@ __global__ void bwd_gs_kernel(const T* P, T* G, const T* delta, int64_t N, int64
     G[i] = (G[i] - delta[i / C]) * P[i];
 }
 
-// gb[v0 + c] = sum_n G[n, c]  (chunked.py:135-136), fixed order per column.
+// gb[v0 + c] = sum_n G[n, c]  (chunked.py:135-136), in a fixed order per column: a block of
+// 256 threads takes 32 columns; thread (r, c) of the 8 x 32 sums rows r, r + 8, r + 16, ...
+// (a warp reads 32 consecutive columns of one row), and the 8 row sums of a column are
+// added in r order.
 template <typename T>
 __global__ void colsum_kernel(const T* G, int64_t N, int64_t C, void* gb, int gdt, int64_t v0) {
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < C;
-       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    T s = 0;
-    for (int64_t n = 0; n < N; ++n) s += G[n * C + c];
-    store_d(gb, gdt, v0 + c, static_cast<double>(s));
+  __shared__ T part[8][33];
+  const int cl = threadIdx.x % 32, r = threadIdx.x / 32;
+  const int64_t c = blockIdx.x * 32LL + cl;
+  T s = 0;
+  if (c < C) {
+#pragma unroll 8
+    for (int64_t n = r; n < N; n += 8) s += G[n * C + c];
+  }
+  part[r][cl] = s;
+  __syncthreads();
+  if (r == 0 && c < C) {
+    T t = part[0][cl];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) t += part[i][cl];
+    store_d(gb, gdt, v0 + c, static_cast<double>(t));
   }
 }
 
@@ -301,19 +620,14 @@ __global__ void zero_rows_kernel(void* dst, int dt, int64_t rows, int64_t cols, 
     store_d(dst, dt, (i / cols) * ld + i % cols, 0.0);
 }
 
-inline unsigned grid_for(int64_t n, int threads = 256) {
-  int64_t g = ceil_div(n, threads);
-  if (g < 1) g = 1;
-  if (g > 4096) g = 4096;
-  return static_cast<unsigned>(g);
-}
 
 // ---------------------------------------------------------------------------------------- host
 size_t fwd_workspace(const swvr_problem& p) {
   const size_t es = p.compute_dtype == SWVR_F64 ? 8 : 4;
   const int64_t C = p.chunk < p.vocab ? p.chunk : (p.vocab > 0 ? p.vocab : 1);
+  const size_t part = es == 4 ? align_up(4 * splitk_floats(p.n_tokens, p.embed_dim), 256) : 0;  // P.E split K
   return align_up(es * p.n_tokens * C, 256) + 2 * align_up(es * p.n_tokens, 256) +
-         align_up(es * p.n_tokens * p.embed_dim, 256) + 256;
+         align_up(es * p.n_tokens * p.embed_dim, 256) + part + 256;
 }
 
 template <typename T>
@@ -329,6 +643,8 @@ static int fwd_impl(const swvr_problem& p, void* m_out, void* l_out, void* acc_o
   T* l = l_out ? static_cast<T*>(l_out) : reinterpret_cast<T*>(w);
   w += align_up(sizeof(T) * N, 256);
   T* acc = acc_out ? static_cast<T*>(acc_out) : reinterpret_cast<T*>(w);
+  w += align_up(sizeof(T) * N * D, 256);
+  float* part = sizeof(T) == 4 ? reinterpret_cast<float*>(w) : nullptr;  // split-K partials of P.E
   const T* h = static_cast<const T*>(p.h);
   const T* W = static_cast<const T*>(p.W);
   const T* E = static_cast<const T*>(p.E);
@@ -336,12 +652,11 @@ static int fwd_impl(const swvr_problem& p, void* m_out, void* l_out, void* acc_o
   fwd_init_kernel<T><<<grid_for(N * D > N ? N * D : N), 256, 0, st>>>(m, l, acc, N, D);
   for (int64_t v0 = 0; v0 < V; v0 += C) {
     const int64_t c = (V - v0) < C ? (V - v0) : C;
-    cudaError_t e = gemm<T>(st, N, c, K, static_cast<T>(p.logit_scale), h, p.ldh, 1, W + v0 * p.ldw, 1, p.ldw, T(0),
-                            S, adt, c, 1);
+    cudaError_t e = gemm_bias<T>(st, N, c, K, static_cast<T>(p.logit_scale), h, p.ldh, 1, W + v0 * p.ldw, 1, p.ldw,
+                                 S, adt, p.bias, p.bias_dtype, v0);
     if (e != cudaSuccess) return SWVR_ERR_CUDA;
-    if (p.bias) add_bias_kernel<T><<<grid_for(N * c), 256, 0, st>>>(S, N, c, p.bias, p.bias_dtype, v0);
     if (N > 0) fwd_update_kernel<T><<<static_cast<unsigned>(N), 256, 0, st>>>(S, c, m, l, acc, D);
-    e = gemm<T>(st, N, D, c, T(1), S, c, 1, E + v0 * p.lde, p.lde, 1, T(1), acc, adt, D, 1);
+    e = gemm_split<T>(st, N, D, c, T(1), S, c, 1, E + v0 * p.lde, p.lde, 1, T(1), acc, adt, D, 1, part);
     if (e != cudaSuccess) return SWVR_ERR_CUDA;
   }
   if (O) fwd_finish_kernel<T><<<grid_for(N * D > N ? N * D : N), 256, 0, st>>>(m, l, acc, O, lse, N, D);
@@ -376,6 +691,7 @@ size_t bwd_workspace(const swvr_problem& p, const swvr_grads& g) {
   const int64_t C = p.chunk < p.vocab ? p.chunk : (p.vocab > 0 ? p.vocab : 1);
   size_t b = 2 * align_up(es * p.n_tokens * C, 256) + align_up(es * p.n_tokens, 256);
   if (g.grad_h && !g.grad_h_acc) b += align_up(es * p.n_tokens * p.hidden, 256);
+  if (es == 4 && g.grad_E) b += align_up(4 * splitk_floats(C, p.embed_dim), 256);  // dE split K
   return b + 256;
 }
 
@@ -395,6 +711,8 @@ static int bwd_impl(const swvr_problem& p, const swvr_grads& g, void* ws, cudaSt
   T* delta = reinterpret_cast<T*>(w);
   w += align_up(sizeof(T) * N, 256);
   T* dh = g.grad_h_acc ? static_cast<T*>(g.grad_h_acc) : reinterpret_cast<T*>(w);
+  if (g.grad_h && !g.grad_h_acc) w += align_up(sizeof(T) * N * K, 256);
+  float* part = sizeof(T) == 4 ? reinterpret_cast<float*>(w) : nullptr;  // split-K partials (bwd_workspace)
   const T* h = static_cast<const T*>(p.h);
   const T* W = static_cast<const T*>(p.W);
   const T* E = static_cast<const T*>(p.E);
@@ -412,20 +730,22 @@ static int bwd_impl(const swvr_problem& p, const swvr_grads& g, void* ws, cudaSt
   for (int64_t v0 = 0; v0 < V; v0 += C) {
     const int64_t c = (V - v0) < C ? (V - v0) : C;
     // P = exp(s h W_c^T + b_c - lse)  (chunked.py:132)
-    if (gemm<T>(st, N, c, K, s, h, p.ldh, 1, W + v0 * p.ldw, 1, p.ldw, T(0), S, adt, c, 1) != cudaSuccess)
+    if (gemm_bias<T>(st, N, c, K, s, h, p.ldh, 1, W + v0 * p.ldw, 1, p.ldw, S, adt, p.bias, p.bias_dtype, v0) !=
+        cudaSuccess)
       return SWVR_ERR_CUDA;
-    if (p.bias) add_bias_kernel<T><<<grid_for(N * c), 256, 0, st>>>(S, N, c, p.bias, p.bias_dtype, v0);
     bwd_p_kernel<T><<<grid_for(N * c), 256, 0, st>>>(S, lse, N, c);
     // G = (gO E_c^T - delta) * P  (chunked.py:134)
     if (gemm<T>(st, N, c, D, T(1), gO, D, 1, E + v0 * p.lde, 1, p.lde, T(0), G, adt, c, 1) != cudaSuccess)
       return SWVR_ERR_CUDA;
     bwd_gs_kernel<T><<<grid_for(N * c), 256, 0, st>>>(S, G, delta, N, c);
-    if (need_b) colsum_kernel<T><<<grid_for(c), 256, 0, st>>>(G, N, c, g.grad_bias, g.grad_bias_dtype, v0);
+    if (need_b)
+      colsum_kernel<T><<<static_cast<unsigned>(ceil_div(c, 32)), 256, 0, st>>>(G, N, c, g.grad_bias, g.grad_bias_dtype,
+                                                                              v0);
     // gE_c = P^T gO  (chunked.py:137-138)
     if (need_E &&
-        gemm<T>(st, c, D, N, T(1), S, 1, c, gO, D, 1, T(0), static_cast<char*>(g.grad_E) +
-                    static_cast<size_t>(v0 * g.ld_grad_E) * dtype_size(g.grad_E_dtype),
-                g.grad_E_dtype, g.ld_grad_E, 1) != cudaSuccess)
+        gemm_split<T>(st, c, D, N, T(1), S, 1, c, gO, D, 1, T(0), static_cast<char*>(g.grad_E) +
+                           static_cast<size_t>(v0 * g.ld_grad_E) * dtype_size(g.grad_E_dtype),
+                       g.grad_E_dtype, g.ld_grad_E, 1, part) != cudaSuccess)
       return SWVR_ERR_CUDA;
     // gH += s G W_c ; gW_c = s G^T h  (chunked.py:142-150)
     if (need_h && gemm<T>(st, N, K, c, s, G, c, 1, W + v0 * p.ldw, p.ldw, 1, T(1), dh, adt, K, 1) != cudaSuccess)

@@ -59,8 +59,8 @@ def test_fused_norm_matches_the_oracle(dtype, tol, affine):
     O, lse, grads = _run(x, w, W, E, b, eps, scale, gO, glse)
     Or, lr, gr = _oracle(x, w, W, E, b, eps, scale, gO, glse)
     assert rel_err(O, Or) < tol and rel_err(lse, lr) < tol
-    # LSE near 10: fp32 rounding alone is ~1e-6 absolute
-    assert np.max(np.abs(npy(lse) - lr)) < {torch.bfloat16: 1e-2, torch.float32: 1e-5, torch.float64: 1e-9}[dtype]
+    # LSE near 10: 1e-4 absolute is the fp32 contract's 1e-5 relative (test_cuda.py:65)
+    assert np.max(np.abs(npy(lse) - lr)) < {torch.bfloat16: 1e-2, torch.float32: 1e-4, torch.float64: 1e-9}[dtype]
     for name, a, r in zip(["gx", "gw", "gW", "gE", "gb"], grads, gr):
         if r is None:
             assert a is None, name
