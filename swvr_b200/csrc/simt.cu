@@ -314,15 +314,25 @@ __global__ void __launch_bounds__(256, 2) gemm_tf32x3_kernel(int64_t M, int64_t 
       if (gm >= M) continue;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        const int64_t gn0 = n0 + wn + j * 8 + 2 * q;
+        float v[2];
 #pragma unroll
         for (int e1 = 0; e1 < 2; ++e1) {
-          const int64_t gn = n0 + wn + j * 8 + 2 * q + e1;
-          if (gn >= N) continue;
-          const int64_t off = gm * scm + gn * scn;
-          float v = alpha * acc[i][j][e2 * 2 + e1];
-          if (beta != 0.f) v += beta * load_f(C, cdt, off);
-          if (cbias) v += load_f(cbias, cbias_dt, gn);  // the score bias of column gn (the S GEMM)
-          store_f(C, cdt, off, v);
+          const int64_t gn = gn0 + e1;
+          v[e1] = alpha * acc[i][j][e2 * 2 + e1];
+          if (gn < N) {
+            if (beta != 0.f) v[e1] += beta * load_f(C, cdt, gm * scm + gn * scn);
+            if (cbias) v[e1] += load_f(cbias, cbias_dt, gn);  // the score bias of column gn (the S GEMM)
+          }
+        }
+        const int64_t off = gm * scm + gn0 * scn;
+        float* dst = static_cast<float*>(C) + off;
+        if (cdt == SWVR_F32 && scn == 1 && gn0 + 1 < N && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+          *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+        } else {
+#pragma unroll
+          for (int e1 = 0; e1 < 2; ++e1)
+            if (gn0 + e1 < N) store_f(C, cdt, off + e1 * scn, v[e1]);
         }
       }
     }
