@@ -20,8 +20,9 @@
  *     attributes guarded by a mutex.
  *   - Compute dtypes: SWVR_BF16 / SWVR_F16 run the tcgen05 tensor-core kernels (fp32
  *     accumulation); SWVR_F32 / SWVR_F64 run the exact path (fp32 GEMMs as three-term
- *     split-TF32 tensor-core products with fp32-level error, fp64 on the CUDA cores).  O, LSE and the
- *     softmax state are fp64 for SWVR_F64 compute and fp32 otherwise (the accumulation dtype).
+ *     split-TF32 tensor-core products with fp32-level error, fp64 on the CUDA cores).  O,
+ *     LSE and the softmax state are fp64 for SWVR_F64 compute and fp32 otherwise (the
+ *     accumulation dtype).
  */
 #ifndef SWVR_B200_H
 #define SWVR_B200_H
