@@ -153,9 +153,10 @@ __global__ void __launch_bounds__(256) gemm_kernel(int64_t M, int64_t N, int64_t
 
 // fp32 GEMM on the tensor cores at fp32 accuracy: each operand is split into a TF32 head and
 // the TF32 rounding of its remainder, x = hi(x) + lo(x), and the product takes the three
-// terms lo·hi + hi·lo + hi·hi in fp32 accumulation (the lo·lo term, ~2^-22 relative, is
-// dropped): about 2^-21 relative error per product, against 2^-24 for an fp32 FMA and 2^-11
-// for plain TF32.  128 x 128 block tiles, 32-deep K tiles in a 3-stage cp.async ring (the
+// terms lo·hi + hi·lo + hi·hi (the lo·lo term, ~2^-22 relative, is dropped): about 2^-21
+// relative error per product, against 2^-24 for an fp32 FMA and 2^-11 for plain TF32.  Each
+// 8-deep K step's terms are summed from zero and added to the running sum in fp32
+// round-to-nearest, so the MMA's own rounding toward zero does not accumulate over K.  128 x 128 block tiles, 32-deep K tiles in a 3-stage cp.async ring (the
 // CUDA-core kernel above, one 8-deep step ahead, waits on its global loads), eight warps of
 // 64 x 32 as 4 x 4 warp-level m16n8k8 TF32 MMAs; the operands are split as the fragments
 // are read.  Each operand is staged in its own global layout: a K-contiguous tile as rows of
@@ -281,14 +282,14 @@ __global__ void __launch_bounds__(256, 2) gemm_tf32x3_kernel(int64_t M, int64_t 
     const float* bs = Bs + (kt % STAGES) * B_WORDS;
 #pragma unroll
     for (int kk = 0; kk < TK; kk += 8) {
-      uint32_t bh[4][2], bl[4][2];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        split_tf32(b_at(bs, kk + q, wn + j * 8 + g), bh[j][0], bl[j][0]);
-        split_tf32(b_at(bs, kk + q + 4, wn + j * 8 + g), bh[j][1], bl[j][1]);
-      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
+        uint32_t bh[4][2], bl[4][2];  // re-split per m tile: 16 fewer live registers
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          split_tf32(b_at(bs, kk + q, wn + j * 8 + g), bh[j][0], bl[j][0]);
+          split_tf32(b_at(bs, kk + q + 4, wn + j * 8 + g), bh[j][1], bl[j][1]);
+        }
         const int r = wm + i * 16 + g;
         uint32_t ah[4], al[4];
         split_tf32(a_at(as, r, kk + q), ah[0], al[0]);
@@ -297,9 +298,15 @@ __global__ void __launch_bounds__(256, 2) gemm_tf32x3_kernel(int64_t M, int64_t 
         split_tf32(a_at(as, r + 8, kk + q + 4), ah[3], al[3]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          mma_tf32(acc[i][j], al, bh[j]);  // small terms first
-          mma_tf32(acc[i][j], ah, bl[j]);
-          mma_tf32(acc[i][j], ah, bh[j]);
+          // the three terms of this 8-deep K step start from zero and are added to the running
+          // sum in fp32 round-to-nearest: the MMA's own accumulation rounds toward zero, which
+          // over a long K (thousands of steps) would bias the sum by ~1e-5 relative
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_tf32(d, al, bh[j]);  // small terms first
+          mma_tf32(d, ah, bl[j]);
+          mma_tf32(d, ah, bh[j]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[i][j][e] += d[e];
         }
       }
     }

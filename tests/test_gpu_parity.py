@@ -125,6 +125,26 @@ def test_fp32_no_tf32_is_exact():
         assert rel_err(a, r) < 1e-5, rel_err(a, r)
 
 
+@pytest.mark.parametrize("N,K,V,D,chunk", [
+    (2048, 256, 4096, 64, 1024),   # aligned: every GEMM on the split-TF32 kernel, dE and P.E split in K
+    (1000, 200, 3000, 36, 1000),   # ragged tiles and K splits with a short last range
+    (513, 130, 2001, 10, 700),     # unaligned rows: the CUDA-core kernel for some GEMMs
+])
+def test_fp32_split_tf32_gemms_are_exact(N, K, V, D, chunk):
+    """The fp32 path's GEMMs (three-term split-TF32 tensor-core products, split in K where the
+    output is narrow, the score bias in the GEMM's epilogue; CUDA-core fallback where the
+    operands cannot be staged 16 bytes at a time) against the fp64 oracle at the fp32
+    contract's 1e-5 (test_cuda.py:57-65)."""
+    inputs = make_gpu(N, K, V, D, torch.float32, seed=9)
+    g = torch.Generator().manual_seed(10)
+    gO, glse = torch.randn(N, D, generator=g).cuda(), torch.randn(N, generator=g).cuda()
+    O, lse = swvr.softmax_readout(*inputs, chunk_size=chunk, logit_scale=0.9)
+    grads = torch.autograd.grad((O * gO).sum() + (lse * glse).sum(), inputs)
+    Or, lr, gr = oracle_eager(*inputs, 0.9, gO, glse)
+    for name, a, r in zip(["O", "lse", "gh", "gW", "gE", "gb"], [O, lse, *grads], [Or, lr, *gr]):
+        assert rel_err(a, r) < 1e-5, (name, rel_err(a, r))
+
+
 def test_autocast_with_fp32_params():
     """test_cuda.py:68-77: autocast bf16 with fp32 parameters keeps fp32 grads."""
     N, K, V, D = 256, 256, 4000, 16
